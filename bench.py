@@ -1,0 +1,398 @@
+"""Benchmark of the fused tied LM-head cross-entropy (forward + backward).
+
+Default workload: config 4 of the path's specification (the headline):
+N = 32768 tokens (4 x 8192), d = 4096, V = 128256, fp16, h unit-RMS rows from
+N(0,1), E ~ N(0, 0.02^2), labels ~ U[0, V). One "step" is one forward and
+backward of the tied head over those N tokens. With --gpus P > 1 (launched by
+torchrun, one rank per GPU) the vocabulary is sharded P ways and the total
+work stays fixed (strong scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4|c3|c2]
+    python bench.py --impl reference ...   # the reference's CPU algorithm
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "tied LM-head+CE fwd+bwd tokens/s (V=128256,d=4096) at 1–8 B200; % TC peak"
+DATASHEET_DENSE_F16_TFLOPS = 2250.0
+DATASHEET_DENSE_TF32_TFLOPS = 1100.0
+
+CONFIGS = {
+    "c4": dict(workload="config 4: large-vocab fused tied CE fwd+bwd (headline)", n=32768, d=4096,
+               v=128256, dtype="float16", unit_rms=True, batch=4, seq=8192),
+    "c3": dict(workload="config 3: fused tied CE fwd+bwd", n=16384, d=2048, v=32000, dtype="float16",
+               unit_rms=True, batch=16, seq=1024),
+    "c2": dict(workload="config 2: standalone fused tied CE fwd+bwd, fp32 on TF32", n=8192, d=768,
+               v=50257, dtype="float32", unit_rms=False, batch=8, seq=1024),
+}
+DTYPE_TAG = {"float16": "f16", "float32": "f32", "bfloat16": "bf16"}
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["bf16_tflops"], d["bf16_tflops_sustained"], d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def _profile_traffic(config_name):
+    """DRAM bytes per launch of the forward GEMM from the committed ncu summary, if any."""
+    p = REPO / "profiles" / f"tc_gemm_ce_fwd_{config_name}.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("dram_bytes_per_launch_full_size")
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id):
+        self.bus_id = (bus_id or "").lower()
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 10:
+                continue
+            if self.bus_id and self.bus_id[-12:] not in parts[1].lower():
+                continue
+            rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, val in zip(names, r[6:10]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def _dist_setup(gpus):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if gpus > 1 and world != gpus:
+        raise SystemExit(f"--gpus {gpus} needs torchrun with {gpus} ranks (WORLD_SIZE={world})")
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return rank, local, world
+
+
+def cpu_reference_sample(cfg, seconds=12.0, max_rows=4096):
+    """Times the reference's CPU algorithm (oracle restatement, NumPy/BLAS fp32,
+    all host threads) on a row sample of the workload; returns a callable step
+    and the sample description."""
+    import numpy as np
+
+    from oracle import tied_ce_oracle as orc
+
+    rng = np.random.default_rng(1234)
+    e = (rng.standard_normal((cfg["v"], cfg["d"]), dtype=np.float32) * np.float32(0.02))
+
+    def make(rows):
+        h = rng.standard_normal((rows, cfg["d"]), dtype=np.float32)
+        if cfg["unit_rms"]:
+            h /= np.sqrt(np.mean(h * h, axis=1, keepdims=True))
+        y = rng.integers(0, cfg["v"], rows, dtype=np.int64)
+        return h, y
+
+    def run(h, y):
+        loss, hh, ww, logits, mx, se = orc.tied_forward(h, e, y, np.float32)
+        orc.tied_backward(1.0, hh, ww, y, logits, mx, se)
+
+    rows = 32
+    h, y = make(rows)
+    t0 = time.perf_counter()
+    run(h, y)
+    dt = time.perf_counter() - t0
+    rows = int(min(max_rows, max(32, rows * seconds / max(dt, 1e-3))))
+    rows = max(32, rows // 32 * 32)
+    h, y = make(rows)
+    sample = (f"{rows} of {cfg['n']} token rows at full d={cfg['d']}, V={cfg['v']}; reference algorithm "
+              f"(oracle/tied_ce_oracle.py restating NimbleML/kernels/fused_*crossentropy.py) in NumPy "
+              f"fp32 with all BLAS threads (the reference's fp16 NumPy path has no BLAS)")
+    return (lambda: run(h, y)), rows, sample
+
+
+def run_reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    step, rows, sample = cpu_reference_sample(cfg)
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    t = statistics.mean(times)
+    value = rows / t
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["workload"], "n_tokens": cfg["n"], "d_model": cfg["d"], "vocab": cfg["v"],
+                   "sample_rows": rows, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def launches_per_step(cfg, world, slab_bytes):
+    """Kernels of libnimbleml_tied_ce.so launched by one step on one rank."""
+    n, d = cfg["n"], cfg["d"]
+    v_local = -(-cfg["v"] // world)
+    es = 4 if cfg["dtype"] == "float32" else 2
+    ldn = -(-n // 64) * 64
+    cols = (slab_bytes or (1 << 30)) // (2 * es * ldn)
+    cols = max(256, cols // 256 * 256)
+    cols = min(cols, -(-v_local // 256) * 256)
+    n_slabs = -(-v_local // cols)
+    k = 2 + 1 + 2 + 3 * n_slabs  # fwd GEMM + row reduce, combine, 2 transposes, 3 GEMMs per slab
+    if cfg["dtype"] == "float32":
+        k += 4  # tf32 rounding copies in forward and backward
+    return k, n_slabs
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args, cfg)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from nimbleml_b200.kernels import fused_tied_crossentropy as k
+    from nimbleml_b200 import vocab_parallel as vp
+    from nimbleml_b200.losses.cross_entropy import CrossEntropyLoss
+
+    rank, local, world = _dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dtype = getattr(torch, cfg["dtype"])
+    n, d, v = cfg["n"], cfg["d"], cfg["v"]
+    group = dist.group.WORLD if world > 1 else None
+    v_off, v_local = vp.shard_range(v, rank, world)
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)  # identical h / labels on every rank
+    h = torch.randn((n, d), generator=gen, device=dev, dtype=torch.float32)
+    if cfg["unit_rms"]:
+        h = h * torch.rsqrt(h.pow(2).mean(dim=1, keepdim=True))
+    h = h.to(dtype).contiguous()
+    labels = torch.randint(0, v, (n,), generator=gen, device=dev, dtype=torch.int64)
+    gen_e = torch.Generator(device=dev)
+    gen_e.manual_seed(99 + rank)
+    e_local = (torch.randn((v_local, d), generator=gen_e, device=dev) * 0.02).to(dtype).contiguous()
+    ign = k._NO_IGNORE
+    ones = torch.ones(1, device=dev)
+
+    fwd_ev = []
+
+    def step(record=False):
+        if record:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        part = k.shard_forward(h, e_local, labels, v_off)
+        if record:
+            b.record()
+            fwd_ev.append((a, b))
+        stats3 = vp.gather_shard_stats(part, group)
+        _, _, lse, loss, valid = k.combine(stats3, labels, v, ign)
+        st = k.TiedCEStats(lse=lse, valid_count=valid, ignore_index=ign, vocab_size=v, vocab_offset=v_off)
+        dh, de = k.shard_backward(ones, h, e_local, labels, st,
+                                  grad_hidden_dtype=torch.float32 if world > 1 else None)
+        if world > 1:
+            vp.reduce_grad_hidden(dh, group)
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    assert k.check_status(dev) == 0
+    bus = None
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+    except Exception:
+        pass
+    sampler = ClockSampler(bus) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    torch.cuda.reset_peak_memory_stats(dev)
+    mem0 = torch.cuda.memory_allocated(dev)
+    barrier()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(args.steps):
+        step(record=True)
+    t_end.record()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    elapsed = t_start.elapsed_time(t_end) / 1e3
+    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_ev)
+    peak_extra = torch.cuda.max_memory_allocated(dev) - mem0
+    assert k.check_status(dev) == 0
+    if world > 1:
+        t = torch.tensor([elapsed, fwd_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed, fwd_ms = float(t[0]), float(t[1])
+
+    # ---- end to end through the public API: host inputs, H2D copy, loss D2H.
+    e2e = None
+    if not args.no_e2e:
+        h_host = h.cpu().pin_memory()
+        y_host = labels.cpu().pin_memory()
+        w_param = e_local.clone().requires_grad_(True)
+        head = vp.VocabParallelTiedHead(None, v, group=group, shard=w_param) if world > 1 else None
+        lossfn = CrossEntropyLoss()
+
+        def e2e_step():
+            hd = h_host.to(dev, non_blocking=True).requires_grad_(True)
+            yd = y_host.to(dev, non_blocking=True)
+            w_param.grad = None
+            if head is None:
+                loss = lossfn.forward_tied(hd.view(cfg["batch"], cfg["seq"], d), w_param, yd)
+            else:
+                loss = head.loss(hd, yd)
+            loss.backward()
+            return float(loss)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        barrier()
+        te = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([te], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            te = float(t[0])
+        e2e = {"value": n * args.steps / te, "unit": "tokens/s",
+               "h2d_bytes_per_step": h_host.numel() * h_host.element_size() + y_host.numel() * 8,
+               "d2h_bytes_per_step": 4 if world == 1 else 4}
+
+    if rank != 0:
+        dist.barrier() if world > 1 else None
+        dist.destroy_process_group() if world > 1 else None
+        return
+
+    burst, sustained, hbm, peak_kind = _peaks()
+    step_s = elapsed / args.steps
+    flops_step_rank = 8.0 * n * d * v_local
+    flops_fwd_launch = 2.0 * n * d * v_local
+    fwd_tflops = flops_fwd_launch / (fwd_ms / 1e3) / 1e12
+    step_tflops = flops_step_rank / step_s / 1e12
+    datasheet = DATASHEET_DENSE_TF32_TFLOPS if cfg["dtype"] == "float32" else DATASHEET_DENSE_F16_TFLOPS
+    k_launch, n_slabs = launches_per_step(cfg, world, k.SLAB_BYTES)
+    traffic = _profile_traffic(args.config) if world == 1 else None
+    line = {
+        "metric": METRIC, "value": n / step_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": DTYPE_TAG[cfg["dtype"]], "data": "synthetic",
+        "config": {"workload": cfg["workload"], "n_tokens": n, "batch": cfg["batch"], "seq_len": cfg["seq"],
+                   "d_model": d, "vocab": v, "parallelism": f"vocab-sharded x{world}" if world > 1 else "1 GPU",
+                   "l2": "inputs larger than L2 (h %.0f MB, E %.0f MB), no flush" % (
+                       n * d * h.element_size() / 1e6, v * d * h.element_size() / 1e6),
+                   "backward_slabs": n_slabs},
+        "roofline": {"bound": "tensor", "kernel": "tc_gemm_tn_kernel<EPI_CE_FWD> (+ row reduce)",
+                     "achieved": fwd_tflops, "peak": sustained, "unit": "TFLOP/s",
+                     "frac": fwd_tflops / sustained, "peak_kind": f"{peak_kind} sustained bf16 cuBLAS",
+                     "traffic": traffic, "flops_per_launch": flops_fwd_launch,
+                     "step_tflops_per_gpu": step_tflops, "step_frac_of_measured": step_tflops / sustained,
+                     "step_frac_of_datasheet_dense": step_tflops / datasheet},
+        "gpu_launches": k_launch * args.steps,
+        "clocks": clocks,
+        "memory": {"peak_extra_bytes": int(peak_extra), "materialised_logits_bytes": n * v * h.element_size(),
+                   "reference_style_peak_bytes": 3 * n * v * h.element_size()},
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        step_fn, rows, sample = cpu_reference_sample(cfg)
+        step_fn()
+        t0 = time.perf_counter()
+        step_fn()
+        tc = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": rows / tc, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                "sample": sample}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

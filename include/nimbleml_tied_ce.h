@@ -1,0 +1,142 @@
+/*
+ * nimbleml_tied_ce.h — C ABI of the B200 fused tied LM-head cross-entropy.
+ *
+ * Plain pointers and sizes only: every pointer argument is a device address on
+ * the current CUDA device unless stated otherwise, `stream` is a cudaStream_t
+ * passed as void* (NULL = legacy default stream), and every entry point
+ * returns 0 on success or a negative NIMBLE_ERR_* code. The message for the
+ * last failure on the calling thread is available from
+ * nimble_tied_ce_last_error().
+ *
+ * Ownership: the caller allocates every output and the workspace; no entry
+ * point allocates or frees device memory. Inputs are read-only and must be
+ * C-contiguous row-major. Launches are asynchronous on `stream`; nothing
+ * synchronises the device.
+ *
+ * Layout of the path (N tokens, d hidden, V vocabulary, P vocab shards):
+ *   hidden  (N, d)        compute dtype
+ *   weights (V_local, d)  compute dtype, rows [v_offset, v_offset + V_local)
+ *                         of the tied embedding matrix E
+ *   labels  (N,)          int64 global class ids, or ignore_index
+ *
+ * Reference interface this library replaces (NimbleML, Python/NumPy/CuPy):
+ *   NimbleML/kernels/fused_tied_crossentropy.py:8-24   forward  (h @ E^T, CE)
+ *   NimbleML/kernels/fused_tied_crossentropy.py:27-48  backward (G @ E, G^T @ h)
+ *   NimbleML/kernels/fused_crossentropy.py:14-30       row max / sum-exp / lse
+ *   NimbleML/kernels/fused_crossentropy.py:33-50       softmax - onehot
+ *   NimbleML/losses/_ce_prepare.py:46-69               ignore_index filtering
+ * The reference's pybind11 device-pointer entry points follow the same
+ * convention of raw addresses plus sizes (native/src/module.cpp:231-284).
+ */
+#ifndef NIMBLEML_TIED_CE_H
+#define NIMBLEML_TIED_CE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NIMBLE_API __attribute__((visibility("default")))
+#else
+#define NIMBLE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of hidden / weights (the compute dtype) and of outputs. */
+enum {
+  NIMBLE_DTYPE_F32 = 0,  /* fp32 storage, tcgen05 kind::tf32 with RN rounding */
+  NIMBLE_DTYPE_F16 = 1,  /* fp16, tcgen05 kind::f16, fp32 accumulate        */
+  NIMBLE_DTYPE_BF16 = 2  /* bf16, tcgen05 kind::f16, fp32 accumulate        */
+};
+
+/* Return codes. Device-side conditions are reported through `status`. */
+enum {
+  NIMBLE_OK = 0,
+  NIMBLE_ERR_INVALID_ARG = -1,  /* bad shape, dtype, alignment or null pointer */
+  NIMBLE_ERR_WORKSPACE = -2,    /* workspace smaller than the size query      */
+  NIMBLE_ERR_CUDA = -3,         /* a CUDA runtime / driver call failed          */
+  NIMBLE_ERR_UNSUPPORTED = -4   /* no sm_100 device or no driver entry point    */
+};
+
+/* Bits OR-ed into the device status word by the kernels. */
+enum {
+  NIMBLE_STATUS_BAD_LABEL = 1,     /* a label outside [0, V) that is not ignore_index */
+  NIMBLE_STATUS_WAIT_TIMEOUT = 2   /* a bounded device wait gave up (kernel aborted)  */
+};
+
+/* 1 when a compute-capability 10.x device is visible, else 0. Mirrors the
+ * reference's availability flags (native/src/module.cpp:13-17,221-227). */
+NIMBLE_API int nimble_tied_ce_available(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+NIMBLE_API const char* nimble_tied_ce_last_error(void);
+
+/* Bytes of workspace nimble_tied_ce_forward needs for these sizes. */
+NIMBLE_API int nimble_tied_ce_forward_workspace_size(int64_t n_tokens, int64_t d_model, int64_t v_local,
+                                          int dtype, size_t* bytes);
+
+/* Forward on one vocab shard (P = 1: the whole vocabulary, v_offset = 0).
+ * Replaces the logits GEMM + row statistics of
+ * NimbleML/kernels/fused_tied_crossentropy.py:8-24 and
+ * NimbleML/kernels/fused_crossentropy.py:14-30, without an N x V buffer.
+ * Writes per token, over this shard's columns only:
+ *   shard_max[i]    = max_j  s_ij            (s = h . E^T, fp32 accumulate)
+ *   shard_sumexp[i] = sum_j exp(s_ij - shard_max[i])
+ *   shard_target[i] = s_i,label  if label lies in this shard, else 0
+ * Rows whose label equals ignore_index still get max / sumexp. */
+NIMBLE_API int nimble_tied_ce_forward(const void* hidden, const void* weights, const int64_t* labels,
+                           int64_t n_tokens, int64_t d_model, int64_t v_local, int64_t v_offset,
+                           int dtype, float* shard_max, float* shard_sumexp, float* shard_target,
+                           void* workspace, size_t workspace_bytes, int* status, void* stream);
+
+/* Merges n_shards shard statistics (each array laid out [n_shards][n_tokens])
+ * into the global per-token statistics and the mean loss over valid rows —
+ * the lse / gather / mean of NimbleML/kernels/fused_crossentropy.py:23-29
+ * with the valid-row mean of NimbleML/losses/cross_entropy.py:124-148.
+ *   out_max[i], out_sumexp[i]: global row max and sum-exp (fp32)
+ *   out_lse[i]  = out_max[i] + log(out_sumexp[i])
+ *   out_loss[0] = sum_{valid i} (lse_i - s_i,label) / n_valid   (0 if none)
+ *   out_valid_count[0] = n_valid as float
+ * The loss sum is a fixed-order reduction: identical inputs give identical
+ * bits on every rank. Labels outside [0, vocab_size) that are not
+ * ignore_index set NIMBLE_STATUS_BAD_LABEL in *status and count as ignored. */
+NIMBLE_API int nimble_tied_ce_combine(const float* shard_max, const float* shard_sumexp,
+                           const float* shard_target, int n_shards, const int64_t* labels,
+                           int64_t n_tokens, int64_t vocab_size, int64_t ignore_index,
+                           float* out_max, float* out_sumexp, float* out_lse, float* out_loss,
+                           float* out_valid_count, int* status, void* stream);
+
+/* Bytes of workspace nimble_tied_ce_backward needs. `slab_bytes` bounds the
+ * per-slab gradient tiles (0 = library default, 1 GiB); the backward walks
+ * the shard in vocab slabs whose G buffers fit that budget. */
+NIMBLE_API int nimble_tied_ce_backward_workspace_size(int64_t n_tokens, int64_t d_model, int64_t v_local,
+                                           int dtype, size_t slab_bytes, size_t* bytes);
+
+/* Backward on one vocab shard. Replaces
+ * NimbleML/kernels/fused_tied_crossentropy.py:27-48 and
+ * NimbleML/kernels/fused_crossentropy.py:33-50: recomputes the logits of
+ * this shard, forms G = (softmax - onehot) * grad_scale / n_valid with the
+ * global lse, and computes
+ *   grad_hidden  (N, d)        = G . E_shard   (this shard's partial sum)
+ *   grad_weights (V_local, d)  = G^T . h       (complete for the shard)
+ * grad_scale and valid_count are DEVICE fp32 scalars (no host sync).
+ * Rows with label == ignore_index get G = 0, hence an exactly-zero
+ * grad_hidden row (NimbleML/losses/cross_entropy.py:181-184).
+ * grad_*_dtype selects the output element type (NIMBLE_DTYPE_*); with
+ * accumulate_grad_weights != 0 the result is added to grad_weights
+ * (NimbleML/utils/tensor.py:334-350 accumulation of the tied grad). */
+NIMBLE_API int nimble_tied_ce_backward(const float* grad_scale, const void* hidden, const void* weights,
+                            const int64_t* labels, const float* lse, const float* valid_count,
+                            int64_t n_tokens, int64_t d_model, int64_t v_local, int64_t v_offset,
+                            int64_t ignore_index, int dtype, void* grad_hidden,
+                            int grad_hidden_dtype, void* grad_weights, int grad_weights_dtype,
+                            int accumulate_grad_weights, size_t slab_bytes, void* workspace,
+                            size_t workspace_bytes, int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NIMBLEML_TIED_CE_H */

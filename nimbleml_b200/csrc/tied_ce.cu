@@ -1,0 +1,985 @@
+// tied_ce.cu — B200 (sm_100a) fused tied LM-head cross-entropy.
+//
+// The reference computes, on CuPy/NumPy (NimbleML/kernels/fused_tied_crossentropy.py:8-48,
+// NimbleML/kernels/fused_crossentropy.py:14-50):
+//   forward : S = h E^T (N x V, materialised); m = rowmax S; s = sum exp(S - m);
+//             lse = m + log s; loss = mean_i (lse_i - S_i,y_i)
+//   backward: G = (exp(S - m) / s - onehot(y)) * grad_scale / N
+//             dh = G E ; dE = G^T h
+// Here nothing N x V is ever stored:
+//   forward : one persistent tcgen05 GEMM over (token block x vocab tile)
+//             tiles whose epilogue reduces each TMEM accumulator row to a
+//             (max, sum-exp) pair and gathers the target logit; a row reduce
+//             merges the per-tile pairs; a combine kernel merges vocab shards
+//             and forms lse and the loss.
+//   backward: per vocab slab of the shard, the same GEMM recomputes the
+//             logits and its epilogue writes G (and G^T) for that slab only;
+//             two more tcgen05 GEMMs give dE rows of the slab (complete) and
+//             add the slab's share of dh.
+// All GEMMs are "TN": C[M x N] = A[M x K] . B[N x K]^T with K-major operands
+// staged by TMA (128-byte swizzle) into a shared-memory ring and fp32
+// accumulators double-buffered in TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "nimbleml_tied_ce.h"
+#include "sm100_ptx.cuh"
+
+namespace nimble {
+
+// ------------------------------------------------------------------ tiling
+constexpr int kBM = 128;          // accumulator rows per tile (TMEM lanes)
+constexpr int kBN = 256;          // accumulator columns per tile
+constexpr int kBKBytes = 128;     // one 128-byte swizzle row of K per stage
+constexpr int kStages = 4;        // shared-memory ring depth
+constexpr int kABytes = kBM * kBKBytes;  // 16 KiB
+constexpr int kBBytes = kBN * kBKBytes;  // 32 KiB
+constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kTmemCols = 2 * kBN;  // two accumulators
+constexpr int kSmemBytes = kStages * (kABytes + kBBytes) + 1024 /*align*/ + 256 /*barriers*/;
+constexpr float kLog2e = 1.4426950408889634f;
+
+enum Epi : int { EPI_CE_FWD = 0, EPI_CE_GRAD = 1, EPI_STORE = 2 };
+
+struct EpiParams {
+  // Shared by the cross-entropy epilogues.
+  const int64_t* labels;   // [M] global class ids
+  int64_t col_origin;      // global class id of B row 0
+  int64_t ignore_index;
+  // EPI_CE_FWD
+  float2* part;            // [n_tiles][M] per-tile (max, sum-exp)
+  float* tgt;              // [M] target logit, written by the owning tile
+  // EPI_CE_GRAD
+  const float* lse;        // [M]
+  void* g;                 // [M][ldg]    G * gscale, compute dtype
+  int64_t ldg;
+  void* gt;                // [N][ldgt]   (G * gscale)^T
+  int64_t ldgt;
+  float gscale;
+  // EPI_STORE: out = alpha * (acc + src) (+ out if accum_out)
+  void* out;
+  int64_t ld_out;
+  int out_dtype;
+  const float* src;
+  int64_t ld_src;
+  const float* alpha_num;  // device scalar or null (1)
+  const float* alpha_den;  // device scalar or null (1); alpha = 0 when *den == 0
+  float alpha_mult;
+  int accum_out;
+  int* status;
+};
+
+template <typename T> struct ElemInfo;
+template <> struct ElemInfo<__half> {
+  static constexpr uint32_t kFmt = 0; static constexpr bool kTF32 = false;
+};
+template <> struct ElemInfo<__nv_bfloat16> {
+  static constexpr uint32_t kFmt = 1; static constexpr bool kTF32 = false;
+};
+template <> struct ElemInfo<float> {
+  static constexpr uint32_t kFmt = 2; static constexpr bool kTF32 = true;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int group_m, int& mb, int& nb) {
+  // Groups of `group_m` token blocks sweep the vocab tiles together so the
+  // concurrently resident tiles share A and B blocks in L2.
+  const int per_group = group_m * n_tiles;
+  const int g = t / per_group;
+  const int first_m = g * group_m;
+  const int gsz = min(group_m, m_tiles - first_m);
+  const int r = t - g * per_group;
+  mb = first_m + r % gsz;
+  nb = r / gsz;
+}
+
+template <typename T>
+__device__ __forceinline__ T to_elem(float x);
+template <> __device__ __forceinline__ __half to_elem<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 to_elem<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <> __device__ __forceinline__ float to_elem<float>(float x) { return ptx::round_tf32(x); }
+
+__device__ __forceinline__ uint32_t pack2(__half a, __half b) {
+  return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
+}
+__device__ __forceinline__ uint32_t pack2(__nv_bfloat16 a, __nv_bfloat16 b) {
+  return static_cast<uint32_t>(__bfloat16_as_ushort(a)) |
+         (static_cast<uint32_t>(__bfloat16_as_ushort(b)) << 16);
+}
+
+// Writes 32 consecutive values v[0..31] (scaled already) as elements of T.
+template <typename T>
+__device__ __forceinline__ void store_row32(T* dst, const float (&v)[32]) {
+  if constexpr (sizeof(T) == 2) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u;
+      u.x = pack2(to_elem<T>(v[8 * q + 0]), to_elem<T>(v[8 * q + 1]));
+      u.y = pack2(to_elem<T>(v[8 * q + 2]), to_elem<T>(v[8 * q + 3]));
+      u.z = pack2(to_elem<T>(v[8 * q + 4]), to_elem<T>(v[8 * q + 5]));
+      u.w = pack2(to_elem<T>(v[8 * q + 6]), to_elem<T>(v[8 * q + 7]));
+      d4[q] = u;
+    }
+  } else {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      d4[q] = make_float4(to_elem<T>(v[4 * q]), to_elem<T>(v[4 * q + 1]), to_elem<T>(v[4 * q + 2]),
+                          to_elem<T>(v[4 * q + 3]));
+  }
+}
+
+__device__ __forceinline__ float load_out_elem(const void* p, int64_t i, int dt) {
+  if (dt == NIMBLE_DTYPE_F32) return static_cast<const float*>(p)[i];
+  if (dt == NIMBLE_DTYPE_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+__device__ __forceinline__ void store_out_elem(void* p, int64_t i, int dt, float v) {
+  if (dt == NIMBLE_DTYPE_F32) static_cast<float*>(p)[i] = v;
+  else if (dt == NIMBLE_DTYPE_F16) static_cast<__half*>(p)[i] = __float2half_rn(v);
+  else static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+// ------------------------------------------------------------- the GEMM
+// Persistent, warp-specialised: warp 0 lane 0 issues TMA loads into a
+// kStages ring, warp 1 lane 0 issues tcgen05.mma into one of two TMEM
+// accumulators, warps 2-5 (one thread per accumulator row) run the epilogue
+// of tile i while the MMAs of tile i+1 proceed.
+template <typename T, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
+                  int N, int K, int group_m, EpiParams ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * kABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + kStages * kBBytes);
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* tfull_bar = empty_bar + kStages;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  constexpr int kElem = sizeof(T);
+  constexpr int kBK = kBKBytes / kElem;           // K elements per stage
+  constexpr int kUK = 32 / kElem;                 // K elements per MMA (32 bytes)
+  constexpr int kKSteps = kBK / kUK;              // MMAs per stage
+  constexpr bool kTF32 = ElemInfo<T>::kTF32;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (M + kBM - 1) / kBM;
+  const int n_tiles = (N + kBN - 1) / kBN;
+  const int tiles = m_tiles * n_tiles;
+  const int k_blocks = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(&full_bar[s], 1);
+      ptx::mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tfull_bar[a], 1);
+      ptx::mbar_init(&tempty_bar[a], 4);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      ptx::prefetch_tmap(&tmA);
+      ptx::prefetch_tmap(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;  // bit s: stage s has a load outstanding-or-done
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, m_tiles, n_tiles, group_m, mb, nb);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!ptx::mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+          ptx::mbar_arrive_expect_tx(&full_bar[stage], kABytes + kBBytes);
+          ptx::tma_load_2d(sA + stage * kABytes, &tmA, &full_bar[stage], kb * kBK, mb * kBM);
+          ptx::tma_load_2d(sB + stage * kBBytes, &tmB, &full_bar[stage], kb * kBK, nb * kBN);
+          issued |= 1u << stage;
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // Let every load already issued land before the CTA can exit: the
+        // most recent phase of each stage is `phase` for stages below the
+        // cursor and `phase ^ 1` at or above it.
+        for (int s = 0; s < kStages; ++s) {
+          if (!(issued & (1u << s))) continue;
+          const uint32_t par = (s < stage) ? phase : (phase ^ 1);
+          const uint64_t t0 = ptx::globaltimer_ns();
+          while (!ptx::mbar_try_wait(&full_bar[s], par) && ptx::globaltimer_ns() - t0 < ptx::kWaitLimitNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = ptx::idesc_f32acc(ElemInfo<T>::kFmt, kBM, kBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t aphase = (it >> 1) & 1;
+        if (!ptx::mbar_wait(&tempty_bar[acc], aphase ^ 1, abort_flag)) { ok = false; break; }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kBN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!ptx::mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const uint64_t adesc = ptx::sdesc_k_sw128(ptx::smem_u32(sA + stage * kABytes));
+          const uint64_t bdesc = ptx::sdesc_k_sw128(ptx::smem_u32(sB + stage * kBBytes));
+#pragma unroll
+          for (int k = 0; k < kKSteps; ++k) {
+            // +2 in the start-address field = +32 bytes along K inside the
+            // 128-byte swizzle row.
+            ptx::umma<kTF32>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          ptx::umma_commit(&empty_bar[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        ptx::umma_commit(&tfull_bar[acc]);
+      }
+      if (!ok) {
+        // Drain: wait until every MMA issued so far has finished.
+        ptx::umma_commit(drain_bar);
+        const uint64_t t0 = ptx::globaltimer_ns();
+        while (!ptx::mbar_try_wait(drain_bar, 0) && ptx::globaltimer_ns() - t0 < ptx::kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------- epilogue
+    const int wq = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_t = wq * 32 + lane;
+    float alpha = 1.0f;
+    if constexpr (EPI == EPI_STORE) {
+      const float num = ep.alpha_num ? *ep.alpha_num : 1.0f;
+      const float den = ep.alpha_den ? *ep.alpha_den : 1.0f;
+      alpha = (den != 0.0f) ? num / den * ep.alpha_mult : 0.0f;
+    }
+    int it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      int mb, nb;
+      tile_coords(t, m_tiles, n_tiles, group_m, mb, nb);
+      const int acc = it & 1;
+      const uint32_t aphase = (it >> 1) & 1;
+      bool ok = ptx::mbar_wait(&tfull_bar[acc], aphase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      ptx::tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kBN;
+      const int64_t row = static_cast<int64_t>(mb) * kBM + row_t;
+      const bool row_ok = row < M;
+      const int ncols = min(kBN, N - nb * kBN);
+      const int64_t col0_tile = static_cast<int64_t>(nb) * kBN;
+
+      if constexpr (EPI == EPI_CE_FWD) {
+        const int64_t lab = row_ok ? ep.labels[row] : INT64_MIN;
+        const int64_t rel = (lab == INT64_MIN) ? -1 : lab - ep.col_origin - col0_tile;
+        const int tcol = (rel >= 0 && rel < ncols) ? static_cast<int>(rel) : -1;
+        float mrun = -INFINITY, srun = 0.0f, tval = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          if (c * 32 >= ncols) break;
+          uint32_t r[32];
+          __syncwarp();
+          ptx::tmem_ld_32cols(tbase + c * 32, r);
+          ptx::tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          const int nv = ncols - c * 32;
+          if (nv < 32) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j >= nv) v[j] = -INFINITY;
+          }
+          float cm = v[0];
+#pragma unroll
+          for (int j = 1; j < 32; ++j) cm = fmaxf(cm, v[j]);
+          const float mnew = fmaxf(mrun, cm);
+          const float ml2 = mnew * kLog2e;
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            s0 += ptx::ex2(fmaf(v[j], kLog2e, -ml2));
+            s1 += ptx::ex2(fmaf(v[j + 1], kLog2e, -ml2));
+          }
+          srun = srun * ptx::ex2((mrun - mnew) * kLog2e) + (s0 + s1);
+          mrun = mnew;
+          const int jt = tcol - c * 32;
+          if (static_cast<unsigned>(jt) < 32u) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j == jt) tval = v[j];
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+        if (row_ok) {
+          ep.part[static_cast<int64_t>(nb) * M + row] = make_float2(mrun, srun);
+          if (tcol >= 0) ep.tgt[row] = tval;
+        }
+      } else if constexpr (EPI == EPI_CE_GRAD) {
+        const int64_t lab = row_ok ? ep.labels[row] : ep.ignore_index;
+        const bool live = row_ok && lab != ep.ignore_index;
+        const int64_t rel = live ? lab - ep.col_origin - col0_tile : -1;
+        const int tcol = (rel >= 0 && rel < ncols) ? static_cast<int>(rel) : -1;
+        const float lse_l2 = live ? ep.lse[row] * kLog2e : 0.0f;
+        const float gs = live ? ep.gscale : 0.0f;
+        T* g = static_cast<T*>(ep.g);
+        T* gt = static_cast<T*>(ep.gt);
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          if (c * 32 >= ncols) break;
+          uint32_t r[32];
+          __syncwarp();
+          ptx::tmem_ld_32cols(tbase + c * 32, r);
+          ptx::tmem_wait_ld();
+          const int jt = tcol - c * 32;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float p = ptx::ex2(fmaf(__uint_as_float(r[j]), kLog2e, -lse_l2));
+            if (j == jt) p -= 1.0f;
+            v[j] = p * gs;
+          }
+          const int64_t col = col0_tile + c * 32;
+          const int nv = min(32, ncols - c * 32);
+          if (row_ok) store_row32<T>(g + row * ep.ldg + col, v);
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nv) gt[(col + j) * ep.ldgt + row] = to_elem<T>(v[j]);
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+      } else {  // EPI_STORE
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          if (c * 32 >= ncols) break;
+          uint32_t r[32];
+          __syncwarp();
+          ptx::tmem_ld_32cols(tbase + c * 32, r);
+          ptx::tmem_wait_ld();
+          if (!row_ok) continue;
+          const int64_t col = col0_tile + c * 32;
+          const int nv = min(32, ncols - c * 32);
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (nv == 32) {
+            if (ep.src) {
+              const float4* s4 = reinterpret_cast<const float4*>(ep.src + row * ep.ld_src + col);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 a = s4[q];
+                v[4 * q] += a.x; v[4 * q + 1] += a.y; v[4 * q + 2] += a.z; v[4 * q + 3] += a.w;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= alpha;
+            if (ep.out_dtype == NIMBLE_DTYPE_F32) {
+              float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(ep.out) + row * ep.ld_out + col);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                if (ep.accum_out) {
+                  const float4 a = o4[q];
+                  o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
+                }
+                o4[q] = o;
+              }
+            } else {
+              uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(ep.out) + row * ep.ld_out + col);
+              const bool f16 = ep.out_dtype == NIMBLE_DTYPE_F16;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                float w[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) w[e] = v[8 * q + e];
+                if (ep.accum_out) {
+                  const uint4 a = o4[q];
+                  const uint32_t av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const uint16_t lo = av[e] & 0xFFFF, hi = av[e] >> 16;
+                    w[2 * e] += f16 ? __half2float(__ushort_as_half(lo)) : __bfloat162float(__ushort_as_bfloat16(lo));
+                    w[2 * e + 1] += f16 ? __half2float(__ushort_as_half(hi)) : __bfloat162float(__ushort_as_bfloat16(hi));
+                  }
+                }
+                uint4 u;
+                if (f16) {
+                  u.x = pack2(__float2half_rn(w[0]), __float2half_rn(w[1]));
+                  u.y = pack2(__float2half_rn(w[2]), __float2half_rn(w[3]));
+                  u.z = pack2(__float2half_rn(w[4]), __float2half_rn(w[5]));
+                  u.w = pack2(__float2half_rn(w[6]), __float2half_rn(w[7]));
+                } else {
+                  u.x = pack2(__float2bfloat16_rn(w[0]), __float2bfloat16_rn(w[1]));
+                  u.y = pack2(__float2bfloat16_rn(w[2]), __float2bfloat16_rn(w[3]));
+                  u.z = pack2(__float2bfloat16_rn(w[4]), __float2bfloat16_rn(w[5]));
+                  u.w = pack2(__float2bfloat16_rn(w[6]), __float2bfloat16_rn(w[7]));
+                }
+                o4[q] = u;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j >= nv) break;
+              float x = v[j];
+              if (ep.src) x += ep.src[row * ep.ld_src + col + j];
+              x *= alpha;
+              const int64_t oi = row * ep.ld_out + col + j;
+              if (ep.accum_out) x += load_out_elem(ep.out, oi, ep.out_dtype);
+              store_out_elem(ep.out, oi, ep.out_dtype, x);
+            }
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag && ep.status) atomicOr(ep.status, NIMBLE_STATUS_WAIT_TIMEOUT);
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// --------------------------------------------------------- helper kernels
+
+// Merges the per-tile (max, sum-exp) pairs of each row into the shard's row
+// statistics and picks the target logit when the label lies in the shard.
+__global__ void ce_row_reduce_kernel(const float2* __restrict__ part, int n_tiles, const float* __restrict__ tgt,
+                                     const int64_t* __restrict__ labels, int64_t M, int64_t v_offset,
+                                     int64_t v_local, float* __restrict__ out_max, float* __restrict__ out_sumexp,
+                                     float* __restrict__ out_target) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= M) return;
+  float m = -INFINITY, s = 0.0f;
+  for (int t = 0; t < n_tiles; ++t) {
+    const float2 p = part[static_cast<int64_t>(t) * M + row];
+    const float mn = fmaxf(m, p.x);
+    s = s * ptx::ex2((m - mn) * kLog2e) + p.y * ptx::ex2((p.x - mn) * kLog2e);
+    m = mn;
+  }
+  out_max[row] = m;
+  out_sumexp[row] = s;
+  const int64_t lab = labels[row];
+  out_target[row] = (lab >= v_offset && lab < v_offset + v_local) ? tgt[row] : 0.0f;
+}
+
+// Single-block fixed-order merge of shard statistics plus the mean loss.
+constexpr int kCombineThreads = 1024;
+__global__ void __launch_bounds__(kCombineThreads)
+ce_combine_kernel(const float* __restrict__ smax, const float* __restrict__ ssum, const float* __restrict__ stgt,
+                  int P, const int64_t* __restrict__ labels, int64_t M, int64_t V, int64_t ignore_index,
+                  float* __restrict__ out_max, float* __restrict__ out_sumexp, float* __restrict__ out_lse,
+                  float* __restrict__ out_loss, float* __restrict__ out_valid, int* status) {
+  __shared__ double s_loss[kCombineThreads];
+  __shared__ int s_cnt[kCombineThreads];
+  double acc = 0.0;
+  int cnt = 0;
+  int bad = 0;
+  for (int64_t i = threadIdx.x; i < M; i += kCombineThreads) {
+    float m = -INFINITY;
+    for (int p = 0; p < P; ++p) m = fmaxf(m, smax[p * M + i]);
+    float s = 0.0f, t = 0.0f;
+    for (int p = 0; p < P; ++p) {
+      s += ssum[p * M + i] * expf(smax[p * M + i] - m);
+      t += stgt[p * M + i];
+    }
+    const float lse = m + logf(s);
+    if (out_max) out_max[i] = m;
+    if (out_sumexp) out_sumexp[i] = s;
+    out_lse[i] = lse;
+    const int64_t lab = labels[i];
+    if (lab != ignore_index) {
+      if (lab < 0 || lab >= V) {
+        bad = 1;
+      } else {
+        acc += static_cast<double>(lse) - static_cast<double>(t);
+        ++cnt;
+      }
+    }
+  }
+  s_loss[threadIdx.x] = acc;
+  s_cnt[threadIdx.x] = cnt;
+  if (bad && status) atomicOr(status, NIMBLE_STATUS_BAD_LABEL);
+  __syncthreads();
+  for (int w = kCombineThreads / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) {
+      s_loss[threadIdx.x] += s_loss[threadIdx.x + w];
+      s_cnt[threadIdx.x] += s_cnt[threadIdx.x + w];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const int n = s_cnt[0];
+    out_loss[0] = n > 0 ? static_cast<float>(s_loss[0] / n) : 0.0f;
+    out_valid[0] = static_cast<float>(n);
+  }
+}
+
+// dst[c * ld_dst + r] = src[r * ld_src + c] for an R x C source; fp32 values
+// are rounded to tf32 on the way (the operand the tensor cores will read).
+template <typename T>
+__global__ void transpose_kernel(const T* __restrict__ src, int64_t R, int64_t C, int64_t ld_src,
+                                 T* __restrict__ dst, int64_t ld_dst) {
+  __shared__ T tile[32][33];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 32;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int64_t r = r0 + k, c = c0 + threadIdx.x;
+    if (r < R && c < C) {
+      T x = src[r * ld_src + c];
+      if constexpr (sizeof(T) == 4) x = ptx::round_tf32(x);
+      tile[k][threadIdx.x] = x;
+    }
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int64_t c = c0 + k, r = r0 + threadIdx.x;
+    if (r < R && c < C) dst[c * ld_dst + r] = tile[threadIdx.x][k];
+  }
+}
+
+__global__ void round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = ptx::round_tf32(src[i]);
+}
+
+// ================================================================ host side
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define NIMBLE_CUDA_TRY(expr)                                                             \
+  do {                                                                                    \
+    cudaError_t e_ = (expr);                                                              \
+    if (e_ != cudaSuccess)                                                                \
+      return fail(NIMBLE_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));   \
+  } while (0)
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int elem_size(int dtype) { return dtype == NIMBLE_DTYPE_F32 ? 4 : 2; }
+
+CUtensorMapDataType tmap_dtype(int dtype) {
+  if (dtype == NIMBLE_DTYPE_F32) return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  if (dtype == NIMBLE_DTYPE_F16) return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// Row-major [rows x k] operand with leading dimension `ld` (elements), loaded
+// in boxes of box_rows x (128 bytes of K) with 128-byte swizzle.
+int make_operand_map(CUtensorMap* map, const void* base, int dtype, int64_t k, int64_t rows, int64_t ld,
+                     int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(NIMBLE_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled entry point unavailable");
+  const int es = elem_size(dtype);
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return fail(NIMBLE_ERR_INVALID_ARG, "operand base address is not 16-byte aligned");
+  if ((ld * es) % 16 != 0)
+    return fail(NIMBLE_ERR_INVALID_ARG, "operand row pitch is not a multiple of 16 bytes");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * es)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBKBytes / es), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, tmap_dtype(dtype), 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NIMBLE_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return NIMBLE_OK;
+}
+
+struct DevInfo {
+  int sms = 0;
+  int major = 0;
+};
+
+int device_info(DevInfo* info) {
+  int dev = 0;
+  NIMBLE_CUDA_TRY(cudaGetDevice(&dev));
+  NIMBLE_CUDA_TRY(cudaDeviceGetAttribute(&info->sms, cudaDevAttrMultiProcessorCount, dev));
+  NIMBLE_CUDA_TRY(cudaDeviceGetAttribute(&info->major, cudaDevAttrComputeCapabilityMajor, dev));
+  if (info->major != 10) return fail(NIMBLE_ERR_UNSUPPORTED, "requires a compute capability 10.x (B200) device");
+  return NIMBLE_OK;
+}
+
+// C[M x N] = A[M x K] . B[N x K]^T with the given epilogue.
+template <typename T, int EPI>
+int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N, int64_t K, int dtype,
+                const EpiParams& ep, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return NIMBLE_OK;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(NIMBLE_ERR_INVALID_ARG, "GEMM extent exceeds 2^31");
+  DevInfo di;
+  if (int rc = device_info(&di)) return rc;
+  CUtensorMap ma, mb;
+  if (int rc = make_operand_map(&ma, A, dtype, K, M, lda, kBM)) return rc;
+  if (int rc = make_operand_map(&mb, B, dtype, K, N, ldb, kBN)) return rc;
+  auto kern = tc_gemm_tn_kernel<T, EPI>;
+  NIMBLE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  const int64_t m_tiles = (M + kBM - 1) / kBM, n_tiles = (N + kBN - 1) / kBN;
+  const int64_t tiles = m_tiles * n_tiles;
+  if (tiles > INT32_MAX) return fail(NIMBLE_ERR_INVALID_ARG, "too many tiles");
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, di.sms));
+  const int group_m = 8;
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, static_cast<int>(M), static_cast<int>(N),
+                                                static_cast<int>(K), group_m, ep);
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+template <int EPI>
+int gemm_dispatch(int dtype, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
+                  int64_t K, const EpiParams& ep, cudaStream_t s) {
+  switch (dtype) {
+    case NIMBLE_DTYPE_F16: return launch_gemm<__half, EPI>(A, lda, B, ldb, M, N, K, dtype, ep, s);
+    case NIMBLE_DTYPE_BF16: return launch_gemm<__nv_bfloat16, EPI>(A, lda, B, ldb, M, N, K, dtype, ep, s);
+    case NIMBLE_DTYPE_F32: return launch_gemm<float, EPI>(A, lda, B, ldb, M, N, K, dtype, ep, s);
+  }
+  return fail(NIMBLE_ERR_INVALID_ARG, "unknown dtype");
+}
+
+int launch_transpose(int dtype, const void* src, int64_t R, int64_t C, int64_t ld_src, void* dst, int64_t ld_dst,
+                     cudaStream_t s) {
+  const int64_t gx = (R + 31) / 32, gy = (C + 31) / 32;
+  if (gx > INT32_MAX || gy > 65535) return fail(NIMBLE_ERR_INVALID_ARG, "transpose extent too large");
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), block(32, 8);
+  if (elem_size(dtype) == 4)
+    transpose_kernel<float><<<grid, block, 0, s>>>(static_cast<const float*>(src), R, C, ld_src,
+                                                   static_cast<float*>(dst), ld_dst);
+  else
+    transpose_kernel<uint16_t><<<grid, block, 0, s>>>(static_cast<const uint16_t*>(src), R, C, ld_src,
+                                                      static_cast<uint16_t*>(dst), ld_dst);
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+int launch_round(const float* src, float* dst, int64_t n, cudaStream_t s) {
+  if (n <= 0) return NIMBLE_OK;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
+  round_tf32_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(src, dst, n);
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t x, size_t a = kAlign) { return (x + a - 1) / a * a; }
+int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+// Forward workspace: per-tile pairs, target logits, and (fp32) tf32-rounded
+// copies of the operands.
+struct FwdLayout {
+  size_t part = 0, tgt = 0, hr = 0, er = 0, total = 0;
+};
+FwdLayout fwd_layout(int64_t N, int64_t d, int64_t V, int dtype) {
+  FwdLayout L;
+  const int64_t n_tiles = (V + kBN - 1) / kBN;
+  size_t off = 0;
+  L.part = off; off = align_up(off + sizeof(float2) * n_tiles * N);
+  L.tgt = off; off = align_up(off + sizeof(float) * N);
+  if (dtype == NIMBLE_DTYPE_F32) {
+    L.hr = off; off = align_up(off + sizeof(float) * N * d);
+    L.er = off; off = align_up(off + sizeof(float) * V * d);
+  }
+  L.total = off;
+  return L;
+}
+
+constexpr size_t kDefaultSlabBytes = size_t(1) << 30;
+
+struct BwdLayout {
+  int64_t slab = 0, ldn = 0, ldv = 0, n_slabs = 0;
+  size_t g = 0, gt = 0, ht = 0, et = 0, dh = 0, hr = 0, er = 0, total = 0;
+};
+BwdLayout bwd_layout(int64_t N, int64_t d, int64_t V, int dtype, size_t slab_bytes) {
+  BwdLayout L;
+  const int64_t es = elem_size(dtype);
+  if (slab_bytes == 0) slab_bytes = kDefaultSlabBytes;
+  L.ldn = round_up(N, 64);
+  L.ldv = round_up(V, 64);
+  // G (N x slab) and G^T (slab x ldn) share the slab budget.
+  int64_t cols = static_cast<int64_t>(slab_bytes / (2 * es * std::max<int64_t>(L.ldn, 1)));
+  cols = std::max<int64_t>(kBN, cols / kBN * kBN);
+  cols = std::min<int64_t>(cols, round_up(V, kBN));
+  L.slab = cols;
+  L.n_slabs = (V + cols - 1) / cols;
+  size_t off = 0;
+  L.g = off; off = align_up(off + es * N * cols);
+  L.gt = off; off = align_up(off + es * cols * L.ldn);
+  L.ht = off; off = align_up(off + es * d * L.ldn);
+  L.et = off; off = align_up(off + es * d * L.ldv);
+  if (L.n_slabs > 1) { L.dh = off; off = align_up(off + sizeof(float) * N * d); }
+  if (dtype == NIMBLE_DTYPE_F32) {
+    L.hr = off; off = align_up(off + sizeof(float) * N * d);
+    L.er = off; off = align_up(off + sizeof(float) * V * d);
+  }
+  L.total = off;
+  return L;
+}
+
+int check_common(const void* h, const void* w, const int64_t* labels, int64_t N, int64_t d, int64_t V, int dtype) {
+  if (dtype != NIMBLE_DTYPE_F32 && dtype != NIMBLE_DTYPE_F16 && dtype != NIMBLE_DTYPE_BF16)
+    return fail(NIMBLE_ERR_INVALID_ARG, "dtype must be NIMBLE_DTYPE_F32, F16 or BF16");
+  if (N < 0 || d <= 0 || V <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "sizes must be positive");
+  if ((d * elem_size(dtype)) % 16 != 0)
+    return fail(NIMBLE_ERR_INVALID_ARG, "d_model * element size must be a multiple of 16 bytes");
+  if (N > 0 && (!h || !w || !labels)) return fail(NIMBLE_ERR_INVALID_ARG, "null input pointer");
+  return NIMBLE_OK;
+}
+
+}  // namespace
+}  // namespace nimble
+
+// ================================================================== C ABI
+using namespace nimble;
+
+extern "C" int nimble_tied_ce_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  for (int i = 0; i < n; ++i) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, i) == cudaSuccess && major == 10)
+      return 1;
+  }
+  return 0;
+}
+
+extern "C" const char* nimble_tied_ce_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int nimble_tied_ce_forward_workspace_size(int64_t n_tokens, int64_t d_model, int64_t v_local, int dtype,
+                                                     size_t* bytes) {
+  if (!bytes) return fail(NIMBLE_ERR_INVALID_ARG, "bytes is null");
+  if (n_tokens < 0 || d_model <= 0 || v_local <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "sizes must be positive");
+  *bytes = fwd_layout(n_tokens, d_model, v_local, dtype).total;
+  return NIMBLE_OK;
+}
+
+extern "C" int nimble_tied_ce_forward(const void* hidden, const void* weights, const int64_t* labels, int64_t n_tokens,
+                                      int64_t d_model, int64_t v_local, int64_t v_offset, int dtype, float* shard_max,
+                                      float* shard_sumexp, float* shard_target, void* workspace,
+                                      size_t workspace_bytes, int* status, void* stream) {
+  if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype)) return rc;
+  if (n_tokens == 0) return NIMBLE_OK;
+  if (!shard_max || !shard_sumexp || !shard_target) return fail(NIMBLE_ERR_INVALID_ARG, "null output pointer");
+  const FwdLayout L = fwd_layout(n_tokens, d_model, v_local, dtype);
+  if (!workspace || workspace_bytes < L.total) return fail(NIMBLE_ERR_WORKSPACE, "forward workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const void* A = hidden;
+  const void* B = weights;
+  if (dtype == NIMBLE_DTYPE_F32) {
+    float* hr = reinterpret_cast<float*>(ws + L.hr);
+    float* er = reinterpret_cast<float*>(ws + L.er);
+    if (int rc = launch_round(static_cast<const float*>(hidden), hr, n_tokens * d_model, s)) return rc;
+    if (int rc = launch_round(static_cast<const float*>(weights), er, v_local * d_model, s)) return rc;
+    A = hr;
+    B = er;
+  }
+  EpiParams ep{};
+  ep.labels = labels;
+  ep.col_origin = v_offset;
+  ep.part = reinterpret_cast<float2*>(ws + L.part);
+  ep.tgt = reinterpret_cast<float*>(ws + L.tgt);
+  ep.status = status;
+  if (int rc = gemm_dispatch<EPI_CE_FWD>(dtype, A, d_model, B, d_model, n_tokens, v_local, d_model, ep, s)) return rc;
+  const int n_tiles = static_cast<int>((v_local + kBN - 1) / kBN);
+  ce_row_reduce_kernel<<<static_cast<unsigned>((n_tokens + 255) / 256), 256, 0, s>>>(
+      ep.part, n_tiles, ep.tgt, labels, n_tokens, v_offset, v_local, shard_max, shard_sumexp, shard_target);
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+extern "C" int nimble_tied_ce_combine(const float* shard_max, const float* shard_sumexp, const float* shard_target,
+                                      int n_shards, const int64_t* labels, int64_t n_tokens, int64_t vocab_size,
+                                      int64_t ignore_index, float* out_max, float* out_sumexp, float* out_lse,
+                                      float* out_loss, float* out_valid_count, int* status, void* stream) {
+  if (n_shards <= 0 || n_tokens < 0 || vocab_size <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "bad sizes");
+  if (!out_lse || !out_loss || !out_valid_count) return fail(NIMBLE_ERR_INVALID_ARG, "null output pointer");
+  if (n_tokens > 0 && (!shard_max || !shard_sumexp || !shard_target || !labels))
+    return fail(NIMBLE_ERR_INVALID_ARG, "null input pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ce_combine_kernel<<<1, kCombineThreads, 0, s>>>(shard_max, shard_sumexp, shard_target, n_shards, labels, n_tokens,
+                                                  vocab_size, ignore_index, out_max, out_sumexp, out_lse, out_loss,
+                                                  out_valid_count, status);
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+extern "C" int nimble_tied_ce_backward_workspace_size(int64_t n_tokens, int64_t d_model, int64_t v_local, int dtype,
+                                                      size_t slab_bytes, size_t* bytes) {
+  if (!bytes) return fail(NIMBLE_ERR_INVALID_ARG, "bytes is null");
+  if (n_tokens < 0 || d_model <= 0 || v_local <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "sizes must be positive");
+  *bytes = bwd_layout(n_tokens, d_model, v_local, dtype, slab_bytes).total;
+  return NIMBLE_OK;
+}
+
+extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidden, const void* weights,
+                                       const int64_t* labels, const float* lse, const float* valid_count,
+                                       int64_t n_tokens, int64_t d_model, int64_t v_local, int64_t v_offset,
+                                       int64_t ignore_index, int dtype, void* grad_hidden, int grad_hidden_dtype,
+                                       void* grad_weights, int grad_weights_dtype, int accumulate_grad_weights,
+                                       size_t slab_bytes, void* workspace, size_t workspace_bytes, int* status,
+                                       void* stream) {
+  if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype)) return rc;
+  if (!grad_hidden || !grad_weights || !grad_scale || !lse || !valid_count)
+    return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  for (int dt : {grad_hidden_dtype, grad_weights_dtype})
+    if (dt != NIMBLE_DTYPE_F32 && dt != NIMBLE_DTYPE_F16 && dt != NIMBLE_DTYPE_BF16)
+      return fail(NIMBLE_ERR_INVALID_ARG, "bad output dtype");
+  if ((reinterpret_cast<uintptr_t>(grad_hidden) & 15) || (reinterpret_cast<uintptr_t>(grad_weights) & 15))
+    return fail(NIMBLE_ERR_INVALID_ARG, "gradient outputs must be 16-byte aligned");
+  if ((d_model * elem_size(grad_hidden_dtype)) % 16 || (d_model * elem_size(grad_weights_dtype)) % 16)
+    return fail(NIMBLE_ERR_INVALID_ARG, "d_model * output element size must be a multiple of 16 bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_tokens == 0) {
+    if (!accumulate_grad_weights)
+      NIMBLE_CUDA_TRY(cudaMemsetAsync(grad_weights, 0, elem_size(grad_weights_dtype) * v_local * d_model, s));
+    return NIMBLE_OK;
+  }
+  const BwdLayout L = bwd_layout(n_tokens, d_model, v_local, dtype, slab_bytes);
+  if (!workspace || workspace_bytes < L.total) return fail(NIMBLE_ERR_WORKSPACE, "backward workspace too small");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int64_t es = elem_size(dtype);
+  const void* h = hidden;
+  const void* E = weights;
+  if (dtype == NIMBLE_DTYPE_F32) {
+    float* hr = reinterpret_cast<float*>(ws + L.hr);
+    float* er = reinterpret_cast<float*>(ws + L.er);
+    if (int rc = launch_round(static_cast<const float*>(hidden), hr, n_tokens * d_model, s)) return rc;
+    if (int rc = launch_round(static_cast<const float*>(weights), er, v_local * d_model, s)) return rc;
+    h = hr;
+    E = er;
+  }
+  void* g = ws + L.g;
+  void* gt = ws + L.gt;
+  void* ht = ws + L.ht;
+  void* et = ws + L.et;
+  float* dh_acc = L.n_slabs > 1 ? reinterpret_cast<float*>(ws + L.dh) : nullptr;
+  if (int rc = launch_transpose(dtype, h, n_tokens, d_model, d_model, ht, L.ldn, s)) return rc;
+  if (int rc = launch_transpose(dtype, E, v_local, d_model, d_model, et, L.ldv, s)) return rc;
+
+  // G is stored scaled by 2^15 in fp16 so that softmax probabilities of order
+  // 1/V stay in the normal range; the scale is undone in the dE / dh epilogue.
+  const float gscale = dtype == NIMBLE_DTYPE_F16 ? 32768.0f : 1.0f;
+  for (int64_t sl = 0; sl < L.n_slabs; ++sl) {
+    const int64_t c0 = sl * L.slab;
+    const int64_t vc = std::min<int64_t>(L.slab, v_local - c0);
+    const void* E_sl = static_cast<const uint8_t*>(E) + es * c0 * d_model;
+    // 1) recompute logits of the slab and write G, G^T.
+    EpiParams eg{};
+    eg.labels = labels;
+    eg.col_origin = v_offset + c0;
+    eg.ignore_index = ignore_index;
+    eg.lse = lse;
+    eg.g = g;
+    eg.ldg = L.slab;
+    eg.gt = gt;
+    eg.ldgt = L.ldn;
+    eg.gscale = gscale;
+    eg.status = status;
+    if (int rc = gemm_dispatch<EPI_CE_GRAD>(dtype, h, d_model, E_sl, d_model, n_tokens, vc, d_model, eg, s)) return rc;
+    // 2) dE[c0:c0+vc] = G^T h  (K = tokens).
+    EpiParams ee{};
+    ee.out = static_cast<uint8_t*>(grad_weights) + elem_size(grad_weights_dtype) * c0 * d_model;
+    ee.ld_out = d_model;
+    ee.out_dtype = grad_weights_dtype;
+    ee.alpha_num = grad_scale;
+    ee.alpha_den = valid_count;
+    ee.alpha_mult = 1.0f / gscale;
+    ee.accum_out = accumulate_grad_weights ? 1 : 0;
+    ee.status = status;
+    if (int rc = gemm_dispatch<EPI_STORE>(dtype, gt, L.ldn, ht, L.ldn, vc, d_model, n_tokens, ee, s)) return rc;
+    // 3) dh (+)= G E[c0:c0+vc]  (K = slab columns).
+    EpiParams eh{};
+    eh.status = status;
+    const bool last = sl == L.n_slabs - 1;
+    if (last) {
+      eh.out = grad_hidden;
+      eh.out_dtype = grad_hidden_dtype;
+      eh.alpha_num = grad_scale;
+      eh.alpha_den = valid_count;
+      eh.alpha_mult = 1.0f / gscale;
+    } else {
+      eh.out = dh_acc;
+      eh.out_dtype = NIMBLE_DTYPE_F32;
+      eh.alpha_mult = 1.0f;
+    }
+    eh.ld_out = d_model;
+    eh.src = sl > 0 ? dh_acc : nullptr;
+    eh.ld_src = d_model;
+    const void* et_sl = static_cast<const uint8_t*>(et) + es * c0;
+    if (int rc = gemm_dispatch<EPI_STORE>(dtype, g, L.slab, et_sl, L.ldv, n_tokens, d_model, vc, eh, s)) return rc;
+  }
+  return NIMBLE_OK;
+}

@@ -1,0 +1,124 @@
+"""``CrossEntropyLoss.forward_tied`` on B200 — the autograd node of the path.
+
+Mirrors NimbleML/losses/cross_entropy.py:109-192: one autograd node for the
+tied head ``hidden @ E^T`` plus cross-entropy, mean over the rows whose label
+is not ``ignore_index``, grads for both ``hidden`` and the tied embedding
+weights. The reference's node is a closure on its own ``Tensor``; here it is
+a ``torch.autograd.Function`` whose backward runs the sm_100a kernels, so
+``E.grad`` accumulates with every other use of the tied matrix (the input
+embedding lookup) exactly as ``Tensor._accumulate_grad`` does
+(NimbleML/utils/tensor.py:334-350).
+
+Differences from the reference, each deliberate:
+
+* No logits are saved: the forward keeps (lse, n_valid) per token and the
+  backward recomputes (the reference saves a copy of the N x V logits,
+  cross_entropy.py:152).
+* ``ignore_index`` rows are masked inside the kernels instead of
+  boolean-indexing a copy of ``hidden`` (``filter_ignore_index``,
+  NimbleML/losses/_ce_prepare.py:46-69), so there is no host sync. When every
+  row is ignored the loss is 0 and both grads are exactly zero (the
+  reference returns a detached zero scalar, so no grad is produced at all).
+* ``grad_scale`` (the upstream grad of the loss) is read on the device.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from nimbleml_b200.kernels.fused_tied_crossentropy import (
+    _NO_IGNORE,
+    CHECK_BOUNDS,
+    TiedCEStats,
+    _as_cuda,
+    as_label_indices,
+    check_status,
+    combine,
+    compute_dtype_of,
+    shard_backward,
+    shard_forward,
+)
+
+
+class _TiedCrossEntropy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h2d, weights, labels, ignore_index, vocab_offset, vocab_size, group):
+        from nimbleml_b200 import vocab_parallel
+
+        part = shard_forward(h2d, weights, labels, vocab_offset)
+        stats3 = vocab_parallel.gather_shard_stats(part, group)  # (3, P, N)
+        _, _, lse, loss, valid = combine(stats3, labels, vocab_size, ignore_index)
+        if CHECK_BOUNDS:
+            check_status(h2d.device)
+        ctx.save_for_backward(h2d, weights, labels, lse, valid)
+        ctx.meta = (ignore_index, vocab_offset, vocab_size, group)
+        return loss
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        from nimbleml_b200 import vocab_parallel
+
+        h2d, weights, labels, lse, valid = ctx.saved_tensors
+        ignore_index, vocab_offset, vocab_size, group = ctx.meta
+        stats = TiedCEStats(lse=lse, valid_count=valid, ignore_index=ignore_index,
+                            vocab_size=vocab_size, vocab_offset=vocab_offset)
+        sharded = vocab_parallel.world_size(group) > 1
+        grad_h, grad_w = shard_backward(
+            grad_out, h2d, weights, labels, stats,
+            grad_hidden_dtype=torch.float32 if sharded else None)
+        if sharded:
+            grad_h = vocab_parallel.reduce_grad_hidden(grad_h, group).to(h2d.dtype)
+        if CHECK_BOUNDS:
+            check_status(h2d.device)
+        return grad_h, grad_w, None, None, None, None, None
+
+
+def tied_cross_entropy(hidden2d, weights, labels, ignore_index: Optional[int] = None, *,
+                       vocab_offset: int = 0, vocab_size: Optional[int] = None, group=None):
+    """Functional form: mean CE of ``hidden2d @ weights^T`` against ``labels``.
+
+    With ``group`` set (a torch.distributed process group), ``weights`` is
+    this rank's vocab shard starting at class ``vocab_offset`` of a
+    ``vocab_size`` vocabulary; every rank gets the same loss, the grad of its
+    own shard and the full ``hidden`` grad.
+    """
+    ign = _NO_IGNORE if ignore_index is None else int(ignore_index)
+    if vocab_size is None:
+        vocab_size = weights.shape[0]
+    return _TiedCrossEntropy.apply(hidden2d, weights, labels, ign, int(vocab_offset), int(vocab_size), group)
+
+
+class CrossEntropyLoss:
+    """Subset of NimbleML's ``CrossEntropyLoss`` that the tied head needs."""
+
+    def forward_tied(self, hidden, embedding_weights, labels, ignore_index=None):
+        """Cross-entropy with tied ``hidden @ embedding_weights.T`` logits.
+
+        ``hidden`` is (batch, seq, d_model); returns a 0-d loss tensor in the
+        compute dtype, as the reference's ``Tensor([loss], ())`` coerces it
+        (NimbleML/utils/tensor.py:147-153).
+        """
+        if hidden.ndim != 3:
+            raise ValueError("forward_tied expects hidden of shape (batch, seq, d_model).")
+        batch, seq_len, d_model = hidden.shape
+        row_count = batch * seq_len
+        compute_dtype_of(hidden)
+        if not hidden.is_cuda:
+            raise RuntimeError("forward_tied on B200 needs CUDA tensors; there is no CPU path")
+        h2d = hidden.reshape(row_count, d_model)
+        if not h2d.is_contiguous():
+            h2d = h2d.contiguous()
+        weights = embedding_weights
+        if weights.dtype != hidden.dtype:
+            weights = weights.to(hidden.dtype)
+        if not weights.is_contiguous():
+            weights = weights.contiguous()
+        label_indices = as_label_indices(labels, batch_size=row_count, device=hidden.device)
+        loss = tied_cross_entropy(h2d, weights, label_indices, ignore_index)
+        return loss.to(hidden.dtype)
+
+    __call__ = forward_tied
+
+
+__all__ = ["CrossEntropyLoss", "tied_cross_entropy", "_as_cuda"]

@@ -1,0 +1,89 @@
+"""Vocabulary-parallel tied cross-entropy across the GPUs of one node.
+
+The reference has no distributed code; this is the vocab split the B200
+design adds. Rank r of P owns rows ``[r*Vp, min((r+1)*Vp, V))`` of the tied
+matrix E (Vp = ceil(V / P)). ``hidden`` and the labels are replicated.
+
+* forward: each rank reduces its vocab columns to per-token (max, sum-exp,
+  target) — 12 bytes per token — and one ``all_gather`` exchanges them; every
+  rank then merges the P triples in the same fixed order, so all ranks hold
+  bit-identical lse and loss.
+* backward: each rank recomputes its logits with the global lse, writes the
+  complete grad of its own E rows (no communication) and a partial
+  grad_hidden = G_r . E_r, summed by one fp32 ``all_reduce`` over NCCL.
+
+Collectives go through ``torch.distributed`` (NCCL on GPUs, gloo on CPU for
+the host-logic tests).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def world_size(group=None) -> int:
+    if group is None or not dist.is_available() or not dist.is_initialized():
+        return 1
+    return dist.get_world_size(group)
+
+
+def rank_in(group=None) -> int:
+    if group is None or not dist.is_available() or not dist.is_initialized():
+        return 0
+    return dist.get_rank(group)
+
+
+def shard_range(vocab_size: int, rank: int, world: int) -> Tuple[int, int]:
+    """(vocab_offset, rows) of rank's shard; the last shard may be short."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must lie in [0, world)")
+    per = -(-vocab_size // world)
+    start = min(rank * per, vocab_size)
+    stop = min(start + per, vocab_size)
+    return start, stop - start
+
+
+def gather_shard_stats(part: torch.Tensor, group=None) -> torch.Tensor:
+    """(3, N) local shard statistics -> (3, P, N) statistics of every shard, rank order."""
+    p = world_size(group)
+    if p == 1:
+        return part.unsqueeze(1)
+    part = part.contiguous()
+    out = torch.empty((p * part.shape[0], part.shape[1]), dtype=part.dtype, device=part.device)
+    dist.all_gather_into_tensor(out, part, group=group)
+    return out.view(p, part.shape[0], part.shape[1]).permute(1, 0, 2).contiguous()
+
+
+def reduce_grad_hidden(grad_h: torch.Tensor, group=None) -> torch.Tensor:
+    """Sums the per-shard partial grad_hidden over the group (in place, fp32)."""
+    if world_size(group) > 1:
+        dist.all_reduce(grad_h, op=dist.ReduceOp.SUM, group=group)
+    return grad_h
+
+
+class VocabParallelTiedHead:
+    """Holds this rank's shard of the tied matrix and applies the sharded loss."""
+
+    def __init__(self, full_weights: Optional[torch.Tensor], vocab_size: int, group=None,
+                 shard: Optional[torch.Tensor] = None):
+        self.group = group
+        self.vocab_size = int(vocab_size)
+        self.world = world_size(group)
+        self.rank = rank_in(group)
+        self.vocab_offset, self.rows = shard_range(self.vocab_size, self.rank, self.world)
+        if shard is None:
+            if full_weights is None:
+                raise ValueError("pass full_weights or shard")
+            shard = full_weights[self.vocab_offset:self.vocab_offset + self.rows]
+        if shard.shape[0] != self.rows:
+            raise ValueError(f"shard has {shard.shape[0]} rows, expected {self.rows}")
+        self.weights = shard.contiguous()
+
+    def loss(self, hidden2d: torch.Tensor, labels: torch.Tensor, ignore_index: Optional[int] = None):
+        from nimbleml_b200.losses.cross_entropy import tied_cross_entropy
+
+        return tied_cross_entropy(hidden2d, self.weights, labels, ignore_index,
+                                  vocab_offset=self.vocab_offset, vocab_size=self.vocab_size,
+                                  group=self.group if self.world > 1 else None)

@@ -1,0 +1,163 @@
+"""Generate golden vectors for the tied-CE path by running the REFERENCE itself.
+
+Imports the reference NimbleML package (CPU backend) with its native
+extension compiled from source by ``oracle/Makefile`` and records seeded
+inputs and outputs of
+
+* ``GPT.compute_loss`` + ``backward`` on the tiny GPT of config 1
+  (NimbleML/models/gpt.py:123-137),
+* ``fused_tied_crossentropy_forward / _backward``
+  (NimbleML/kernels/fused_tied_crossentropy.py:8-48) in float32, float64 and
+  float16,
+* ``CrossEntropyLoss.forward_tied`` with ``ignore_index``
+  (NimbleML/losses/cross_entropy.py:109-192),
+
+as ``.npz`` files beside this script. Run in a container that has the
+reference checkout (it is not needed afterwards):
+
+    make -C oracle REF=/root/reference
+    python tests/golden/gen_golden.py --ref /root/reference
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import random
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path.insert(0, str(REPO))
+from oracle.tied_ce_oracle import make_inputs  # noqa: E402
+
+
+def _import_reference(ref: Path):
+    os.environ["NIMBLEML_DEVICE"] = "cpu"
+    sys.path.insert(0, str(REPO / "oracle" / "_ref"))
+    sys.path.insert(0, str(ref))
+    import NimbleML  # noqa: F401
+    from NimbleML.utils import np_backend
+    return np_backend
+
+
+def kernel_case(nb, name, n, d, v, seed, dtype, unit_rms=False, store_inputs=True, force_edges=False):
+    from NimbleML.kernels import fused_tied_crossentropy_backward, fused_tied_crossentropy_forward
+
+    h, e, y = make_inputs(n, d, v, seed=seed, unit_rms=unit_rms)
+    if force_edges:
+        y[0], y[-1] = 0, v - 1
+    out = {"n": n, "d": d, "v": v, "seed": seed, "unit_rms": unit_rms, "labels": y}
+    if store_inputs:
+        out.update(h=h, e=e)
+    if dtype == "float16":
+        # The parity target for fp16: the reference run in float64 on the
+        # fp16-rounded inputs; the reference's own fp16 result is kept for
+        # information (its backward flushes p/N to zero in fp16).
+        h16, e16 = h.astype(np.float16), e.astype(np.float16)
+        nb.set_dtype("float64")
+        loss, hh, ww, logits, mx, se = fused_tied_crossentropy_forward(h16.astype(np.float64),
+                                                                       e16.astype(np.float64), y)
+        gh, gw = fused_tied_crossentropy_backward(1.0, hh, ww, y, logits, mx, se)
+        out.update(loss=loss, max=mx.ravel(), sumexp=se.ravel(), dh=gh, de=gw)
+        nb.set_dtype("float16")
+        loss16, hh, ww, logits, mx, se = fused_tied_crossentropy_forward(h16, e16, y)
+        gh16, gw16 = fused_tied_crossentropy_backward(1.0, hh, ww, y, logits, mx, se)
+        out.update(ref16_loss=loss16, ref16_dh=gh16, ref16_de=gw16)
+    else:
+        nb.set_dtype(dtype)
+        loss, hh, ww, logits, mx, se = fused_tied_crossentropy_forward(h, e, y)
+        gh, gw = fused_tied_crossentropy_backward(1.0, hh, ww, y, logits, mx, se)
+        out.update(loss=loss, max=mx.ravel(), sumexp=se.ravel(), dh=gh, de=gw)
+    out["dtype"] = dtype
+    return name, out
+
+
+def projected(out, seed):
+    """Replace a large dE with fixed projections (the fixture stays small)."""
+    rng = np.random.default_rng(seed + 7)
+    de = np.asarray(out.pop("de"), np.float64)
+    u_d = rng.standard_normal(de.shape[1])
+    u_v = rng.standard_normal(de.shape[0])
+    rows = np.unique(np.concatenate([out["labels"][:16], rng.integers(0, de.shape[0], 16)]))
+    out.update(de_proj_d=de @ u_d, de_proj_v=u_v @ de, de_rows_idx=rows, de_rows=de[rows],
+               de_norm=np.linalg.norm(de))
+    return out
+
+
+def ignore_case(nb, name, b, s, d, v, seed, ignore_index, frac, dtype="float32"):
+    from NimbleML.losses.cross_entropy import CrossEntropyLoss
+    from NimbleML.utils.tensor import Tensor
+
+    nb.set_dtype(dtype)
+    h, e, y = make_inputs(b * s, d, v, seed=seed, ignore_frac=frac, ignore_index=ignore_index)
+    ht = Tensor(h.ravel(), (b, s, d), requires_grad=True)
+    et = Tensor(e.ravel(), (v, d), requires_grad=True)
+    loss = CrossEntropyLoss().forward_tied(ht, et, y.reshape(b, s), ignore_index=ignore_index)
+    loss.backward()
+    dh = np.zeros((b * s, d), np.float32) if ht.grad is None else np.asarray(ht.grad).reshape(b * s, d)
+    de = np.zeros((v, d), np.float32) if et.grad is None else np.asarray(et.grad).reshape(v, d)
+    return name, {"b": b, "s": s, "d": d, "v": v, "seed": seed, "ignore_index": ignore_index,
+                  "h": h, "e": e, "labels": y, "loss": loss.item(), "dh": dh, "de": de,
+                  "grads_present": np.array([ht.grad is not None, et.grad is not None])}
+
+
+def tiny_gpt_case(nb):
+    from NimbleML import GPT, Tensor
+    from NimbleML.losses.cross_entropy import CrossEntropyLoss
+
+    nb.set_dtype("float32")
+    random.seed(0)
+    np.random.seed(0)
+    m = GPT(vocab_size=256, d_model=64, num_heads=4, num_layers=2, max_seq_len=32, fused_blocks=True)
+    rng = np.random.default_rng(1)
+    ids = rng.integers(0, 256, (2, 8), dtype=np.int64)
+    lab = rng.integers(0, 256, (2, 8), dtype=np.int64)
+    loss = m.compute_loss(Tensor.from_int64(ids, (2, 8)), Tensor.from_int64(lab, (2, 8)))
+    loss.backward()
+    model_loss = loss.item()
+    emb_grad_norm = float(np.linalg.norm(m.token_emb.weights.grad))
+    hidden = np.asarray(m._hidden_states(Tensor.from_int64(ids, (2, 8)))._view()).astype(np.float32)
+    e = np.asarray(m.token_emb.weights._view()).astype(np.float32)
+    ht = Tensor(hidden.ravel(), (2, 8, 64), requires_grad=True)
+    et = Tensor(e.ravel(), e.shape, requires_grad=True)
+    head = CrossEntropyLoss().forward_tied(ht, et, lab)
+    head.backward()
+    return "c1_tiny_gpt", {"ids": ids, "labels": lab.ravel(), "model_loss": model_loss,
+                           "model_emb_grad_norm": emb_grad_norm, "h": hidden.reshape(16, 64), "e": e,
+                           "loss": head.item(), "dh": np.asarray(ht.grad).reshape(16, 64),
+                           "de": np.asarray(et.grad).reshape(e.shape)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    nb = _import_reference(Path(args.ref))
+    cases = [
+        tiny_gpt_case(nb),
+        kernel_case(nb, "small_f32", 96, 64, 1000, 11, "float32"),
+        kernel_case(nb, "small_f64", 96, 64, 1000, 11, "float64"),
+        kernel_case(nb, "ragged_f32", 77, 40, 257, 12, "float32", force_edges=True),
+        kernel_case(nb, "tile_multi_f32", 300, 192, 1300, 13, "float32", force_edges=True),
+        kernel_case(nb, "small_f16", 64, 64, 2048, 14, "float16", unit_rms=True),
+        ignore_case(nb, "ignore_f32", 4, 16, 32, 300, 15, -1, 0.25),
+        ignore_case(nb, "all_ignored_f32", 2, 8, 32, 100, 16, -1, 1.01),
+    ]
+    name, c2 = kernel_case(nb, "c2_slice_f32", 64, 768, 50257, 21, "float32", store_inputs=False)
+    cases.append((name, projected(c2, 21)))
+    name, c3 = kernel_case(nb, "c3_slice_f16", 32, 2048, 32000, 31, "float16", unit_rms=True,
+                           store_inputs=False)
+    for k in ("ref16_dh", "ref16_de"):
+        c3.pop(k)
+    cases.append((name, projected(c3, 31)))
+    for name, data in cases:
+        path = HERE / f"{name}.npz"
+        np.savez_compressed(path, **{k: np.asarray(v) for k, v in data.items()})
+        print(f"{path.name}: {path.stat().st_size / 1024:.0f} KiB, loss={float(data['loss']):.6f}")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,282 @@
+"""Parity of the sm_100a tied-CE path against the oracle and the reference's golden vectors.
+
+Tolerances (from the path's specification), relative, rel(a, b) = |a-b|_2 / |b|_2:
+  fp32 inputs (TF32 tensor cores):  loss <= 1e-5, grads <= 1e-3
+  fp16 / bf16 inputs:               loss <= 2e-3, grads <= 1e-2
+fp16/bf16 results are compared with the reference's math run in float64 on
+the same fp16/bf16-rounded inputs (the reference's own fp16 backward flushes
+p/N to zero and is not a usable target).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle import tied_ce_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: (1e-5, 1e-3), torch.float16: (2e-3, 1e-2), torch.bfloat16: (2e-3, 1e-2)}
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+def golden(name):
+    return dict(np.load(GOLDEN / f"{name}.npz"))
+
+
+def to_dev(x, dtype):
+    return torch.as_tensor(np.ascontiguousarray(x)).to("cuda").to(dtype).contiguous()
+
+
+def rounded64(x, dtype):
+    """Host copy of x after rounding to the device compute dtype, as float64."""
+    return torch.as_tensor(np.ascontiguousarray(x)).to(dtype).to(torch.float64).numpy()
+
+
+def run_path(h, e, y, dtype, ignore_index=None, slab_bytes=None, grad_scale=1.0):
+    """Forward + backward through the public kernels (C ABI underneath)."""
+    from nimbleml_b200.kernels import fused_tied_crossentropy as k
+
+    hd, ed = to_dev(h, dtype), to_dev(e, dtype)
+    yd = torch.as_tensor(y).to("cuda")
+    loss, hh, ww, stats, mx, se = k.fused_tied_crossentropy_forward(hd, ed, yd, ignore_index=ignore_index)
+    gs = torch.full((1,), grad_scale, device="cuda")
+    dh, de = k.shard_backward(gs, hh, ww, yd, stats, slab_bytes=slab_bytes)
+    torch.cuda.synchronize()
+    assert k.check_status(hd.device) == 0
+    f = lambda t: t.double().cpu().numpy()
+    return float(loss), f(mx).ravel(), f(se).ravel(), f(stats.lse), f(dh), f(de)
+
+
+@pytest.fixture(autouse=True)
+def _device():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from nimbleml_b200._native_loader import native
+
+    assert native.available(), "needs a compute capability 10.x device"
+    yield
+
+
+@pytest.mark.parametrize("name", ["small_f32", "ragged_f32", "tile_multi_f32"])
+def test_fp32_goldens(name):
+    g = golden(name)
+    lt, gt = TOL[torch.float32]
+    loss, mx, se, lse, dh, de = run_path(g["h"], g["e"], g["labels"], torch.float32)
+    assert abs(loss - float(g["loss"])) <= lt * abs(float(g["loss"]))
+    assert rel(mx, g["max"]) <= 1e-3
+    assert rel(se, g["sumexp"]) <= 1e-3
+    assert rel(dh, g["dh"]) <= gt
+    assert rel(de, g["de"]) <= gt
+
+
+def test_fp16_golden_against_float64_reference():
+    g = golden("small_f16")
+    lt, gt = TOL[torch.float16]
+    loss, mx, se, lse, dh, de = run_path(g["h"], g["e"], g["labels"], torch.float16)
+    assert abs(loss - float(g["loss"])) <= lt * float(g["loss"])
+    assert rel(dh, g["dh"]) <= gt
+    assert rel(de, g["de"]) <= gt
+    # For information: the reference's own fp16 result is far less accurate.
+    print("ref-fp16 dh rel err vs f64:", rel(g["ref16_dh"], g["dh"]), "ours:", rel(dh, g["dh"]))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(1, 8, 16), (257, 64, 513), (300, 136, 1000), (640, 256, 3000)])
+def test_oracle_parity_dtypes_and_ragged_shapes(dtype, shape):
+    n, d, v = shape
+    h, e, y = orc.make_inputs(n, d, v, seed=n + d + v, unit_rms=True)
+    y[0] = 0
+    y[-1] = v - 1
+    lt, gt = TOL[dtype]
+    loss, mx, se, lse, dh, de = run_path(h, e, y, dtype)
+    l64, dh64, de64, mx64, se64 = orc.row_chunked_reference(rounded64(h, dtype), rounded64(e, dtype), y)
+    assert abs(loss - l64) <= lt * l64
+    assert rel(lse, mx64 + np.log(se64)) <= lt
+    assert rel(dh, dh64) <= gt
+    assert rel(de, de64) <= gt
+
+
+def test_multi_slab_backward_matches_single_slab():
+    n, d, v = 384, 128, 2100
+    h, e, y = orc.make_inputs(n, d, v, seed=9, unit_rms=True)
+    one = run_path(h, e, y, torch.float16)
+    # 256-column slabs: 9 slabs, dh accumulated in the fp32 scratch.
+    many = run_path(h, e, y, torch.float16, slab_bytes=2 * 2 * 384 * 256)
+    assert one[0] == many[0]
+    assert rel(many[4], one[4]) < 1e-6
+    assert rel(many[5], one[5]) < 1e-6
+    l64, dh64, de64, _, _ = orc.row_chunked_reference(rounded64(h, torch.float16), rounded64(e, torch.float16), y)
+    assert rel(many[4], dh64) < 1e-2 and rel(many[5], de64) < 1e-2
+
+
+def test_deterministic_bitwise():
+    h, e, y = orc.make_inputs(500, 192, 1500, seed=4, unit_rms=True)
+    a = run_path(h, e, y, torch.float16)
+    b = run_path(h, e, y, torch.float16)
+    assert a[0] == b[0]
+    for x, z in zip(a[1:], b[1:]):
+        assert np.array_equal(x, z)
+
+
+def test_grad_scale_is_applied():
+    h, e, y = orc.make_inputs(130, 64, 700, seed=5, unit_rms=True)
+    a = run_path(h, e, y, torch.float32, grad_scale=1.0)
+    b = run_path(h, e, y, torch.float32, grad_scale=0.25)
+    assert rel(b[4], 0.25 * a[4]) < 1e-6 and rel(b[5], 0.25 * a[5]) < 1e-6
+
+
+@pytest.mark.parametrize("name", ["ignore_f32", "all_ignored_f32"])
+def test_forward_tied_autograd_ignore_index(name):
+    from nimbleml_b200.losses import CrossEntropyLoss
+
+    g = golden(name)
+    b, s, d, v = int(g["b"]), int(g["s"]), int(g["d"]), int(g["v"])
+    ign = int(g["ignore_index"])
+    hid = to_dev(g["h"].reshape(b, s, d), torch.float32).requires_grad_(True)
+    emb = to_dev(g["e"], torch.float32).requires_grad_(True)
+    labels = torch.as_tensor(g["labels"].reshape(b, s)).cuda()
+    loss = CrossEntropyLoss().forward_tied(hid, emb, labels, ignore_index=ign)
+    loss.backward()
+    torch.cuda.synchronize()
+    lt, gt = TOL[torch.float32]
+    assert abs(float(loss) - float(g["loss"])) <= lt * max(1.0, abs(float(g["loss"])))
+    dh = hid.grad.reshape(b * s, d).double().cpu().numpy()
+    de = emb.grad.double().cpu().numpy()
+    ignored = g["labels"] == ign
+    assert np.all(dh[ignored] == 0.0)
+    if ignored.all():
+        assert float(loss) == 0.0 and not dh.any() and not de.any()
+    else:
+        assert rel(dh, g["dh"]) <= gt and rel(de, g["de"]) <= gt
+
+
+def test_tiny_gpt_head_config1():
+    """Config 1: the tiny GPT's hidden states and tied E through forward_tied + backward."""
+    from nimbleml_b200.losses import CrossEntropyLoss
+
+    g = golden("c1_tiny_gpt")
+    hid = to_dev(g["h"].reshape(2, 8, 64), torch.float32).requires_grad_(True)
+    emb = to_dev(g["e"], torch.float32).requires_grad_(True)
+    loss = CrossEntropyLoss().forward_tied(hid, emb, torch.as_tensor(g["labels"].reshape(2, 8)).cuda())
+    loss.backward()
+    lt, gt = TOL[torch.float32]
+    assert abs(float(loss) - float(g["loss"])) <= lt * float(g["loss"])
+    assert rel(hid.grad.reshape(16, 64).cpu().numpy(), g["dh"]) <= gt
+    assert rel(emb.grad.cpu().numpy(), g["de"]) <= gt
+
+
+def test_tied_grad_accumulates_with_embedding_lookup():
+    """E.grad = head grad + lookup grad when E is also the input embedding."""
+    from nimbleml_b200.losses import CrossEntropyLoss
+
+    n, d, v = 64, 64, 500
+    h, e, y = orc.make_inputs(n, d, v, seed=6)
+    emb = to_dev(e, torch.float32).requires_grad_(True)
+    ids = torch.as_tensor(y).cuda()
+    hid = (emb[ids] + to_dev(h, torch.float32)).reshape(4, 16, d)
+    loss = CrossEntropyLoss().forward_tied(hid, emb, torch.roll(ids, 1).reshape(4, 16))
+    loss.backward()
+    emb2 = to_dev(e, torch.float32).requires_grad_(True)
+    hid2 = (emb2[ids] + to_dev(h, torch.float32)).reshape(4, 16, d)
+    logits = hid2.reshape(n, d) @ emb2.T
+    ref = torch.nn.functional.cross_entropy(logits.double(), torch.roll(ids, 1))
+    ref.backward()
+    assert abs(float(loss) - float(ref)) < 1e-5 * float(ref)
+    assert rel(emb.grad.cpu().numpy(), emb2.grad.cpu().numpy()) < 1e-3
+
+
+def test_bad_label_sets_status():
+    from nimbleml_b200.kernels import fused_tied_crossentropy as k
+
+    h, e, y = orc.make_inputs(40, 32, 100, seed=8)
+    y[3] = 100  # == V: out of range, not ignore_index
+    k.fused_tied_crossentropy_forward(to_dev(h, torch.float32), to_dev(e, torch.float32),
+                                      torch.as_tensor(y).cuda())
+    torch.cuda.synchronize()
+    with pytest.raises(ValueError, match="out of range"):
+        k.check_status(torch.device("cuda", torch.cuda.current_device()))
+
+
+@pytest.mark.parametrize("name,dtype", [("c2_slice_f32", torch.float32), ("c3_slice_f16", torch.float16)])
+def test_benchmark_shape_slices_against_reference(name, dtype):
+    g = golden(name)
+    n, d, v = int(g["n"]), int(g["d"]), int(g["v"])
+    h, e, y = orc.make_inputs(n, d, v, seed=int(g["seed"]), unit_rms=bool(g["unit_rms"]))
+    lt, gt = TOL[dtype]
+    loss, mx, se, lse, dh, de = run_path(h, e, y, dtype)
+    assert abs(loss - float(g["loss"])) <= lt * float(g["loss"])
+    assert rel(dh, g["dh"]) <= gt
+    rng = np.random.default_rng(int(g["seed"]) + 7)
+    u_d = rng.standard_normal(d)
+    u_v = rng.standard_normal(v)
+    assert rel(de @ u_d, g["de_proj_d"]) <= gt
+    assert rel(u_v @ de, g["de_proj_v"]) <= gt
+    assert rel(de[g["de_rows_idx"]], g["de_rows"]) <= gt
+
+
+def test_config2_full_size_tf32():
+    """Config 2 at full size (N=8192, d=768, V=50257, fp32/TF32) against the float64 oracle."""
+    n, d, v = 8192, 768, 50257
+    h, e, y = orc.make_inputs(n, d, v, seed=21)
+    loss, mx, se, lse, dh, de = run_path(h, e, y, torch.float32)
+    l64, dh64, de64, mx64, se64 = orc.row_chunked_reference(h, e, y, rows_per_chunk=512)
+    lt, gt = TOL[torch.float32]
+    assert abs(loss - l64) <= lt * l64
+    assert rel(dh, dh64) <= gt
+    assert rel(de, de64) <= gt
+
+
+def test_headline_shape_full_size_properties():
+    """Config 4 at full size (N=32768, d=4096, V=128256, fp16): no N x V buffer,
+    sampled rows against the float64 oracle, and size-independent identities."""
+    from nimbleml_b200.kernels import fused_tied_crossentropy as k
+
+    n, d, v = 32768, 4096, 128256
+    h, e, y = orc.make_inputs(n, d, v, seed=41, unit_rms=True)
+    hd, ed = to_dev(h, torch.float16), to_dev(e, torch.float16)
+    yd = torch.as_tensor(y).cuda()
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    loss, hh, ww, stats, mx, se = k.fused_tied_crossentropy_forward(hd, ed, yd)
+    dh, de = k.shard_backward(torch.ones(1, device="cuda"), hh, ww, yd, stats)
+    torch.cuda.synchronize()
+    assert k.check_status(hd.device) == 0
+    peak_extra = torch.cuda.max_memory_allocated() - base
+    logits_bytes = n * v * 2
+    assert peak_extra < logits_bytes, (peak_extra, logits_bytes)
+    rows = np.random.default_rng(0).choice(n, 48, replace=False)
+    h64 = rounded64(h[rows], torch.float16)
+    e64 = rounded64(e, torch.float16)
+    s = h64 @ e64.T
+    lse64 = np.log(np.exp(s - s.max(1, keepdims=True)).sum(1)) + s.max(1)
+    lse = stats.lse.double().cpu().numpy()
+    assert rel(lse[rows], lse64) < 2e-3
+    # Loss: mean over rows of lse - target; the sampled rows' terms must agree.
+    tgt = s[np.arange(len(rows)), y[rows]]
+    lossd = float(loss)
+    assert np.isfinite(lossd) and abs(lossd - np.log(v)) < 1.0
+    # dh rows: G_row . E with the float64 lse of the row.
+    g = np.exp(s - lse64[:, None])
+    g[np.arange(len(rows)), y[rows]] -= 1.0
+    dh_ref = (g / n) @ e64
+    dhn = dh.double().cpu().numpy()
+    assert rel(dhn[rows], dh_ref) < 1e-2
+    # Sum over the vocab of dE is sum_n (sum_v G_nv) h_n = 0.
+    den = de.double()
+    colsum = den.sum(0).cpu().numpy()
+    assert np.linalg.norm(colsum) < 1e-3 * float(den.norm())
+    # dE rows for sampled classes, rebuilt from h and the device lse.
+    cls = np.random.default_rng(1).choice(v, 8, replace=False)
+    hf = rounded64(h, torch.float16)
+    pc = np.exp(hf @ e64[cls].T - lse[:, None])
+    for j, c in enumerate(cls):
+        pc[y == c, j] -= 1.0
+    de_ref = (pc / n).T @ hf
+    assert rel(den[torch.as_tensor(cls).cuda()].cpu().numpy(), de_ref) < 1e-2
+    _ = tgt
