@@ -169,7 +169,7 @@ def run_reference_arm(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    step, rows, sample = cpu_reference_sample(cfg)
+    step, rows, sample = cpu_reference_sample(cfg, seconds=6.0)
     for _ in range(args.warmup):
         step()
     times = []
@@ -283,7 +283,8 @@ def main():
     assert k.check_status(dev) == 0
     bus = None
     try:
-        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+        pr = torch.cuda.get_device_properties(dev)
+        bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
     except Exception:
         pass
     sampler = ClockSampler(bus) if rank == 0 else None

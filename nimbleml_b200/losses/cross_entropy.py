@@ -46,13 +46,20 @@ class _TiedCrossEntropy(torch.autograd.Function):
     def forward(ctx, h2d, weights, labels, ignore_index, vocab_offset, vocab_size, group):
         from nimbleml_b200 import vocab_parallel
 
+        # The tensor cores read E in the hidden's dtype; fp32 master weights
+        # are cast for the GEMMs but receive an fp32 grad straight from the
+        # kernel epilogue.
+        weights_in_dtype = weights.dtype
+        if weights.dtype != h2d.dtype:
+            weights = weights.to(h2d.dtype)
+        weights = weights.contiguous()
         part = shard_forward(h2d, weights, labels, vocab_offset)
         stats3 = vocab_parallel.gather_shard_stats(part, group)  # (3, P, N)
         _, _, lse, loss, valid = combine(stats3, labels, vocab_size, ignore_index)
         if CHECK_BOUNDS:
             check_status(h2d.device)
         ctx.save_for_backward(h2d, weights, labels, lse, valid)
-        ctx.meta = (ignore_index, vocab_offset, vocab_size, group)
+        ctx.meta = (ignore_index, vocab_offset, vocab_size, group, weights_in_dtype)
         return loss
 
     @staticmethod
@@ -60,13 +67,14 @@ class _TiedCrossEntropy(torch.autograd.Function):
         from nimbleml_b200 import vocab_parallel
 
         h2d, weights, labels, lse, valid = ctx.saved_tensors
-        ignore_index, vocab_offset, vocab_size, group = ctx.meta
+        ignore_index, vocab_offset, vocab_size, group, w_dtype = ctx.meta
         stats = TiedCEStats(lse=lse, valid_count=valid, ignore_index=ignore_index,
                             vocab_size=vocab_size, vocab_offset=vocab_offset)
         sharded = vocab_parallel.world_size(group) > 1
+        grad_w = torch.empty(weights.shape, dtype=w_dtype, device=weights.device)
         grad_h, grad_w = shard_backward(
             grad_out, h2d, weights, labels, stats,
-            grad_hidden_dtype=torch.float32 if sharded else None)
+            grad_hidden_dtype=torch.float32 if sharded else None, grad_weights=grad_w)
         if sharded:
             grad_h = vocab_parallel.reduce_grad_hidden(grad_h, group).to(h2d.dtype)
         if CHECK_BOUNDS:
@@ -110,8 +118,6 @@ class CrossEntropyLoss:
         if not h2d.is_contiguous():
             h2d = h2d.contiguous()
         weights = embedding_weights
-        if weights.dtype != hidden.dtype:
-            weights = weights.to(hidden.dtype)
         if not weights.is_contiguous():
             weights = weights.contiguous()
         label_indices = as_label_indices(labels, batch_size=row_count, device=hidden.device)

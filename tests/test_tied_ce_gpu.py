@@ -108,8 +108,10 @@ def test_multi_slab_backward_matches_single_slab():
     # 256-column slabs: 9 slabs, dh accumulated in the fp32 scratch.
     many = run_path(h, e, y, torch.float16, slab_bytes=2 * 2 * 384 * 256)
     assert one[0] == many[0]
-    assert rel(many[4], one[4]) < 1e-6
-    assert rel(many[5], one[5]) < 1e-6
+    # dh: fp32 partial sums over slabs vs one fp32 accumulation, then fp16
+    # output rounding; dE rows of each slab are computed identically.
+    assert rel(many[4], one[4]) < 2e-4
+    assert np.array_equal(many[5], one[5])
     l64, dh64, de64, _, _ = orc.row_chunked_reference(rounded64(h, torch.float16), rounded64(e, torch.float16), y)
     assert rel(many[4], dh64) < 1e-2 and rel(many[5], de64) < 1e-2
 
@@ -244,7 +246,10 @@ def test_headline_shape_full_size_properties():
     torch.cuda.reset_peak_memory_stats()
     base = torch.cuda.memory_allocated()
     loss, hh, ww, stats, mx, se = k.fused_tied_crossentropy_forward(hd, ed, yd)
-    dh, de = k.shard_backward(torch.ones(1, device="cuda"), hh, ww, yd, stats)
+    # fp32 grad outputs: at N = 32768 and grad_scale = 1 the grads are ~1e-6,
+    # below fp16's normal range (training scales the loss for fp16 grads).
+    dh, de = k.shard_backward(torch.ones(1, device="cuda"), hh, ww, yd, stats, grad_hidden_dtype=torch.float32,
+                              grad_weights=torch.empty((v, d), dtype=torch.float32, device="cuda"))
     torch.cuda.synchronize()
     assert k.check_status(hd.device) == 0
     peak_extra = torch.cuda.max_memory_allocated() - base
