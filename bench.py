@@ -37,6 +37,8 @@ CONFIGS = {
                v=128256, dtype="float16", unit_rms=True, batch=4, seq=8192),
     "c3": dict(workload="config 3: fused tied CE fwd+bwd", n=16384, d=2048, v=32000, dtype="float16",
                unit_rms=True, batch=16, seq=1024),
+    "mid": dict(workload="profiling case: config-4 d with N=4096, V=32768 (inputs > L2)", n=4096, d=4096,
+                v=32768, dtype="float16", unit_rms=True, batch=1, seq=4096),
     "c2": dict(workload="config 2: standalone fused tied CE fwd+bwd, fp32 on TF32", n=8192, d=768,
                v=50257, dtype="float32", unit_rms=False, batch=8, seq=1024),
 }
