@@ -135,6 +135,24 @@ NIMBLE_API int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
                             int accumulate_grad_weights, size_t slab_bytes, void* workspace,
                             size_t workspace_bytes, int* status, void* stream);
 
+/* Allocation-free variant of nimble_tied_ce_forward; no counterpart in the
+ * reference. For callers that cannot allocate device memory (a runtime whose
+ * GPU memory belongs to another framework's pool, or a binding that may only
+ * pass tensors it already holds): the per-tile scratch lives in a fixed
+ * 64 MiB array inside this library, resident on every GPU that loads it until
+ * the process exits. Sizes whose forward workspace
+ * (nimble_tied_ce_forward_workspace_size) exceeds 64 MiB are rejected with
+ * NIMBLE_ERR_INVALID_ARG. Calls no cudaMalloc / cudaFree. The first call on
+ * each device looks up the array's device address, so make it before any
+ * stream capture. All calls share the one array: calls that overlap on the
+ * GPU (different streams, or different host threads on one device) race and
+ * must be serialised by the caller. Results equal nimble_tied_ce_forward's. */
+NIMBLE_API int nimble_tied_ce_forward_noalloc(const void* hidden, const void* weights,
+                                              const int64_t* labels, int64_t n_tokens,
+                                              int64_t d_model, int64_t v_local, int64_t v_offset,
+                                              int dtype, float* shard_max, float* shard_sumexp,
+                                              float* shard_target, int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -10,6 +10,8 @@ Public surface, mirroring the reference's names:
 
 The compute runs in ``libnimbleml_tied_ce.so`` (C ABI, include/nimbleml_tied_ce.h).
 """
-from nimbleml_b200._native_loader import native  # noqa: F401  (fails loudly if unbuilt)
+# The library is loaded by nimbleml_b200._native_loader when the kernels or
+# losses modules are imported (ImportError with the build command if it is
+# missing); the package itself imports without it so the build step can run.
 
 __version__ = "0.1.0"

@@ -44,6 +44,9 @@ SIGNATURES = {
         _c_int,
         [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_vp,
          _c_vp, _c_size, _c_vp, _c_vp]),
+    "nimble_tied_ce_forward_noalloc": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp]),
     "nimble_tied_ce_combine": (
         _c_int,
         [_c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp,

@@ -983,3 +983,60 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
   }
   return NIMBLE_OK;
 }
+
+// ============================================ allocation-free forward variant
+// For callers that cannot allocate device memory at all: e.g. a host runtime
+// whose GPU memory is owned by another framework's pool, or an embedding
+// layer that may only hand over tensors it already holds. The forward's
+// per-tile scratch then lives in this fixed file-scope array instead of a
+// caller workspace. Every GPU that loads this library keeps the array
+// resident until the process exits.
+namespace nimble {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;  // 64 MiB
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device. In host code
+// the symbol is only a host-side stand-in, so the address must be looked up
+// once per device with that device current.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  NIMBLE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(NIMBLE_ERR_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    NIMBLE_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return NIMBLE_OK;
+}
+
+}  // namespace
+}  // namespace nimble
+
+extern "C" int nimble_tied_ce_forward_noalloc(const void* hidden, const void* weights, const int64_t* labels,
+                                              int64_t n_tokens, int64_t d_model, int64_t v_local,
+                                              int64_t v_offset, int dtype, float* shard_max, float* shard_sumexp,
+                                              float* shard_target, int* status, void* stream) {
+  if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype)) return rc;
+  const size_t need = fwd_layout(n_tokens, d_model, v_local, dtype).total;
+  if (need > kNoAllocScratchBytes)
+    return fail(NIMBLE_ERR_INVALID_ARG,
+                "nimble_tied_ce_forward_noalloc: these sizes need " + std::to_string(need) +
+                    " bytes of scratch but the built-in array holds " + std::to_string(kNoAllocScratchBytes) +
+                    " (64 MiB); split the tokens into smaller calls or use nimble_tied_ce_forward");
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // Nothing in the scratch needs to start at zero: every per-tile pair is
+  // written before the row reduce reads it, and a row's target slot is only
+  // read when the tile that owns its label wrote it in this call.
+  return nimble_tied_ce_forward(hidden, weights, labels, n_tokens, d_model, v_local, v_offset, dtype, shard_max,
+                                shard_sumexp, shard_target, scratch, kNoAllocScratchBytes, status, stream);
+}
