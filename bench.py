@@ -199,12 +199,11 @@ def launches_per_step(cfg, world, slab_bytes):
     n, d = cfg["n"], cfg["d"]
     v_local = -(-cfg["v"] // world)
     es = 4 if cfg["dtype"] == "float32" else 2
-    ldn = -(-n // 64) * 64
-    cols = (slab_bytes or (1 << 30)) // (2 * es * ldn)
+    cols = (slab_bytes or (2 << 30)) // (es * n)
     cols = max(256, cols // 256 * 256)
     cols = min(cols, -(-v_local // 256) * 256)
     n_slabs = -(-v_local // cols)
-    k = 2 + 1 + 2 + 3 * n_slabs  # fwd GEMM + row reduce, combine, 2 transposes, 3 GEMMs per slab
+    k = 2 + 1 + 3 * n_slabs  # fwd GEMM + row reduce, combine, 3 GEMMs per slab
     if cfg["dtype"] == "float32":
         k += 4  # tf32 rounding copies in forward and backward
     return k, n_slabs

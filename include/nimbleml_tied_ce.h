@@ -109,7 +109,7 @@ NIMBLE_API int nimble_tied_ce_combine(const float* shard_max, const float* shard
                            float* out_valid_count, int* status, void* stream);
 
 /* Bytes of workspace nimble_tied_ce_backward needs. `slab_bytes` bounds the
- * per-slab gradient tiles (0 = library default, 1 GiB); the backward walks
+ * per-slab gradient tiles (0 = library default, 2 GiB); the backward walks
  * the shard in vocab slabs whose G buffers fit that budget. */
 NIMBLE_API int nimble_tied_ce_backward_workspace_size(int64_t n_tokens, int64_t d_model, int64_t v_local,
                                            int dtype, size_t slab_bytes, size_t* bytes);

@@ -166,12 +166,31 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16 / kind::tf32 with fp32 accumulate,
-// both operands K-major: D format in bits [4,6) (1 = F32), A / B format in
-// [7,10) / [10,13) (0 = F16, 1 = BF16, 2 = TF32), N >> 3 in [17,23),
-// M >> 4 in [24,29).
-__host__ __device__ constexpr uint32_t idesc_f32acc(uint32_t ab_format, uint32_t m, uint32_t n) {
-  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+// Shared-memory matrix descriptor for an MN-major operand tile written by
+// TMA as boxes of (128 bytes of MN) x (K rows), each K row 128 B, consecutive
+// 128-byte MN chunks `chunk_bytes` apart (leading byte offset). 16-bit types
+// use the 128-byte swizzle (layout type 2) with 8-row atoms 1024 B apart
+// along K (stride byte offset); tf32 must use the 128-byte swizzle with
+// 32-byte atoms (layout type 1, TMA mode SWIZZLE_128B_ATOM_32B) whose K atoms
+// are 4 rows, 512 B apart.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t smem_addr, uint32_t chunk_bytes, bool tf32) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((chunk_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((tf32 ? 512u : 1024u) >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(tf32 ? 1u : 2u) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 / kind::tf32 with fp32 accumulate:
+// D format in bits [4,6) (1 = F32), A / B format in [7,10) / [10,13)
+// (0 = F16, 1 = BF16, 2 = TF32), A / B major-ness in bits 15 / 16
+// (0 = K-major, 1 = MN-major), N >> 3 in [17,23), M >> 4 in [24,29).
+__host__ __device__ constexpr uint32_t idesc_f32acc(uint32_t ab_format, uint32_t m, uint32_t n, bool a_mn = false,
+                                                    bool b_mn = false) {
+  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (a_mn ? 1u << 15 : 0u) | (b_mn ? 1u << 16 : 0u) |
+         ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
 // ------------------------------------------------------------------- math

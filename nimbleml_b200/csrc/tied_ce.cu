@@ -13,12 +13,13 @@
 //             merges the per-tile pairs; a combine kernel merges vocab shards
 //             and forms lse and the loss.
 //   backward: per vocab slab of the shard, the same GEMM recomputes the
-//             logits and its epilogue writes G (and G^T) for that slab only;
-//             two more tcgen05 GEMMs give dE rows of the slab (complete) and
-//             add the slab's share of dh.
-// All GEMMs are "TN": C[M x N] = A[M x K] . B[N x K]^T with K-major operands
-// staged by TMA (128-byte swizzle) into a shared-memory ring and fp32
-// accumulators double-buffered in TMEM.
+//             logits and its epilogue writes G for that slab only; two more
+//             tcgen05 GEMMs give dE rows of the slab (complete) and add the
+//             slab's share of dh, reading G, h and E in place (MN-major
+//             operands where the contraction runs along their rows).
+// All GEMMs compute C[M x N] = A[M x K] . B[N x K]^T with operands staged by
+// TMA (128-byte swizzle) into a shared-memory ring and fp32 accumulators
+// double-buffered in TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -64,8 +65,6 @@ struct EpiParams {
   const float* lse;        // [M]
   void* g;                 // [M][ldg]    G * gscale, compute dtype
   int64_t ldg;
-  void* gt;                // [N][ldgt]   (G * gscale)^T
-  int64_t ldgt;
   float gscale;
   // EPI_STORE: out = alpha * (acc + src) (+ out if accum_out)
   void* out;
@@ -157,8 +156,10 @@ __device__ __forceinline__ void store_out_elem(void* p, int64_t i, int dt, float
 // Persistent, warp-specialised: warp 0 lane 0 issues TMA loads into a
 // kStages ring, warp 1 lane 0 issues tcgen05.mma into one of two TMEM
 // accumulators, warps 2-5 (one thread per accumulator row) run the epilogue
-// of tile i while the MMAs of tile i+1 proceed.
-template <typename T, int EPI>
+// of tile i while the MMAs of tile i+1 proceed. kAMN / kBMN select an
+// MN-major A / B operand (the tensor map's inner dimension is then M / N and
+// the tile arrives as 128-byte-wide MN chunks of K rows).
+template <typename T, int EPI, bool kAMN, bool kBMN>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
                   int N, int K, int group_m, EpiParams ep) {
@@ -225,8 +226,22 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!ptx::mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) { ok = false; break; }
           ptx::mbar_arrive_expect_tx(&full_bar[stage], kABytes + kBBytes);
-          ptx::tma_load_2d(sA + stage * kABytes, &tmA, &full_bar[stage], kb * kBK, mb * kBM);
-          ptx::tma_load_2d(sB + stage * kBBytes, &tmB, &full_bar[stage], kb * kBK, nb * kBN);
+          if constexpr (kAMN) {
+#pragma unroll
+            for (int j = 0; j < kBM / kBK; ++j)
+              ptx::tma_load_2d(sA + stage * kABytes + j * kBK * 128, &tmA, &full_bar[stage], mb * kBM + j * kBK,
+                               kb * kBK);
+          } else {
+            ptx::tma_load_2d(sA + stage * kABytes, &tmA, &full_bar[stage], kb * kBK, mb * kBM);
+          }
+          if constexpr (kBMN) {
+#pragma unroll
+            for (int j = 0; j < kBN / kBK; ++j)
+              ptx::tma_load_2d(sB + stage * kBBytes + j * kBK * 128, &tmB, &full_bar[stage], nb * kBN + j * kBK,
+                               kb * kBK);
+          } else {
+            ptx::tma_load_2d(sB + stage * kBBytes, &tmB, &full_bar[stage], kb * kBK, nb * kBN);
+          }
           issued |= 1u << stage;
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
@@ -247,7 +262,11 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = ptx::idesc_f32acc(ElemInfo<T>::kFmt, kBM, kBN);
+      constexpr uint32_t idesc = ptx::idesc_f32acc(ElemInfo<T>::kFmt, kBM, kBN, kAMN, kBMN);
+      // Start-address step (16-byte units) per MMA along K: 32 bytes inside a
+      // K-major swizzle row, or kUK rows of 128 bytes for an MN-major tile.
+      constexpr uint64_t kAStep = kAMN ? kUK * 128 / 16 : 2;
+      constexpr uint64_t kBStep = kBMN ? kUK * 128 / 16 : 2;
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -261,14 +280,13 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!ptx::mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
-          const uint64_t adesc = ptx::sdesc_k_sw128(ptx::smem_u32(sA + stage * kABytes));
-          const uint64_t bdesc = ptx::sdesc_k_sw128(ptx::smem_u32(sB + stage * kBBytes));
+          const uint32_t a_addr = ptx::smem_u32(sA + stage * kABytes);
+          const uint32_t b_addr = ptx::smem_u32(sB + stage * kBBytes);
+          const uint64_t adesc = kAMN ? ptx::sdesc_mn_sw128(a_addr, kBK * 128, kTF32) : ptx::sdesc_k_sw128(a_addr);
+          const uint64_t bdesc = kBMN ? ptx::sdesc_mn_sw128(b_addr, kBK * 128, kTF32) : ptx::sdesc_k_sw128(b_addr);
 #pragma unroll
-          for (int k = 0; k < kKSteps; ++k) {
-            // +2 in the start-address field = +32 bytes along K inside the
-            // 128-byte swizzle row.
-            ptx::umma<kTF32>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < kKSteps; ++k)
+            ptx::umma<kTF32>(d_tmem, adesc + kAStep * k, bdesc + kBStep * k, idesc, (kb | k) != 0 ? 1u : 0u);
           ptx::umma_commit(&empty_bar[stage]);
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
@@ -365,7 +383,6 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         const float lse_l2 = live ? ep.lse[row] * kLog2e : 0.0f;
         const float gs = live ? ep.gscale : 0.0f;
         T* g = static_cast<T*>(ep.g);
-        T* gt = static_cast<T*>(ep.gt);
 #pragma unroll 1
         for (int c = 0; c < kBN / 32; ++c) {
           if (c * 32 >= ncols) break;
@@ -382,13 +399,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             v[j] = p * gs;
           }
           const int64_t col = col0_tile + c * 32;
-          const int nv = min(32, ncols - c * 32);
           if (row_ok) store_row32<T>(g + row * ep.ldg + col, v);
-          if (row_ok) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < nv) gt[(col + j) * ep.ldgt + row] = to_elem<T>(v[j]);
-          }
         }
         ptx::tc_fence_before();
         __syncwarp();
@@ -567,29 +578,6 @@ ce_combine_kernel(const float* __restrict__ smax, const float* __restrict__ ssum
   }
 }
 
-// dst[c * ld_dst + r] = src[r * ld_src + c] for an R x C source; fp32 values
-// are rounded to tf32 on the way (the operand the tensor cores will read).
-template <typename T>
-__global__ void transpose_kernel(const T* __restrict__ src, int64_t R, int64_t C, int64_t ld_src,
-                                 T* __restrict__ dst, int64_t ld_dst) {
-  __shared__ T tile[32][33];
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 32;
-  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 32;
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int64_t r = r0 + k, c = c0 + threadIdx.x;
-    if (r < R && c < C) {
-      T x = src[r * ld_src + c];
-      if constexpr (sizeof(T) == 4) x = ptx::round_tf32(x);
-      tile[k][threadIdx.x] = x;
-    }
-  }
-  __syncthreads();
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int64_t c = c0 + k, r = r0 + threadIdx.x;
-    if (r < R && c < C) dst[c * ld_dst + r] = tile[threadIdx.x][k];
-  }
-}
-
 __global__ void round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t n) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -635,10 +623,12 @@ CUtensorMapDataType tmap_dtype(int dtype) {
   return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 }
 
-// Row-major [rows x k] operand with leading dimension `ld` (elements), loaded
-// in boxes of box_rows x (128 bytes of K) with 128-byte swizzle.
-int make_operand_map(CUtensorMap* map, const void* base, int dtype, int64_t k, int64_t rows, int64_t ld,
-                     int box_rows) {
+// 2-D operand map with 128-byte swizzle. K-major: a row-major [rows x k]
+// matrix, boxes of box_rows x (128 bytes of K). MN-major: a row-major
+// [k x mn] matrix (MN contiguous), boxes of (128 bytes of MN) x (128 / elem
+// K rows). `ld` is the row pitch in elements.
+int make_operand_map(CUtensorMap* map, const void* base, int dtype, bool mn_major, int64_t k, int64_t rows,
+                     int64_t ld, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return fail(NIMBLE_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled entry point unavailable");
   const int es = elem_size(dtype);
@@ -646,12 +636,28 @@ int make_operand_map(CUtensorMap* map, const void* base, int dtype, int64_t k, i
     return fail(NIMBLE_ERR_INVALID_ARG, "operand base address is not 16-byte aligned");
   if ((ld * es) % 16 != 0)
     return fail(NIMBLE_ERR_INVALID_ARG, "operand row pitch is not a multiple of 16 bytes");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  const cuuint32_t chunk = static_cast<cuuint32_t>(kBKBytes / es);
+  cuuint64_t dims[2];
+  cuuint32_t box[2];
+  if (mn_major) {
+    dims[0] = static_cast<cuuint64_t>(rows);
+    dims[1] = static_cast<cuuint64_t>(k);
+    box[0] = chunk;
+    box[1] = chunk;
+  } else {
+    dims[0] = static_cast<cuuint64_t>(k);
+    dims[1] = static_cast<cuuint64_t>(rows);
+    box[0] = chunk;
+    box[1] = static_cast<cuuint32_t>(box_rows);
+  }
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * es)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBKBytes / es), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
+  // MN-major fp32 (read as tf32) needs the 32-byte-atom variant of the
+  // 128-byte swizzle; every other operand uses the plain 128-byte swizzle.
+  const CUtensorMapSwizzle swz = (mn_major && es == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                       : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = fn(map, tmap_dtype(dtype), 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(NIMBLE_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
   return NIMBLE_OK;
@@ -671,8 +677,9 @@ int device_info(DevInfo* info) {
   return NIMBLE_OK;
 }
 
-// C[M x N] = A[M x K] . B[N x K]^T with the given epilogue.
-template <typename T, int EPI>
+// C[M x N] = A[M x K] . B[N x K]^T with the given epilogue. A is stored
+// row-major [M x K] (K-major) or [K x M] (kAMN); likewise B.
+template <typename T, int EPI, bool kAMN, bool kBMN>
 int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N, int64_t K, int dtype,
                 const EpiParams& ep, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return NIMBLE_OK;
@@ -681,9 +688,9 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t 
   DevInfo di;
   if (int rc = device_info(&di)) return rc;
   CUtensorMap ma, mb;
-  if (int rc = make_operand_map(&ma, A, dtype, K, M, lda, kBM)) return rc;
-  if (int rc = make_operand_map(&mb, B, dtype, K, N, ldb, kBN)) return rc;
-  auto kern = tc_gemm_tn_kernel<T, EPI>;
+  if (int rc = make_operand_map(&ma, A, dtype, kAMN, K, M, lda, kBM)) return rc;
+  if (int rc = make_operand_map(&mb, B, dtype, kBMN, K, N, ldb, kBN)) return rc;
+  auto kern = tc_gemm_tn_kernel<T, EPI, kAMN, kBMN>;
   NIMBLE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
   const int64_t m_tiles = (M + kBM - 1) / kBM, n_tiles = (N + kBN - 1) / kBN;
   const int64_t tiles = m_tiles * n_tiles;
@@ -696,30 +703,18 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t 
   return NIMBLE_OK;
 }
 
-template <int EPI>
+template <int EPI, bool kAMN = false, bool kBMN = false>
 int gemm_dispatch(int dtype, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
                   int64_t K, const EpiParams& ep, cudaStream_t s) {
   switch (dtype) {
-    case NIMBLE_DTYPE_F16: return launch_gemm<__half, EPI>(A, lda, B, ldb, M, N, K, dtype, ep, s);
-    case NIMBLE_DTYPE_BF16: return launch_gemm<__nv_bfloat16, EPI>(A, lda, B, ldb, M, N, K, dtype, ep, s);
-    case NIMBLE_DTYPE_F32: return launch_gemm<float, EPI>(A, lda, B, ldb, M, N, K, dtype, ep, s);
+    case NIMBLE_DTYPE_F16:
+      return launch_gemm<__half, EPI, kAMN, kBMN>(A, lda, B, ldb, M, N, K, dtype, ep, s);
+    case NIMBLE_DTYPE_BF16:
+      return launch_gemm<__nv_bfloat16, EPI, kAMN, kBMN>(A, lda, B, ldb, M, N, K, dtype, ep, s);
+    case NIMBLE_DTYPE_F32:
+      return launch_gemm<float, EPI, kAMN, kBMN>(A, lda, B, ldb, M, N, K, dtype, ep, s);
   }
   return fail(NIMBLE_ERR_INVALID_ARG, "unknown dtype");
-}
-
-int launch_transpose(int dtype, const void* src, int64_t R, int64_t C, int64_t ld_src, void* dst, int64_t ld_dst,
-                     cudaStream_t s) {
-  const int64_t gx = (R + 31) / 32, gy = (C + 31) / 32;
-  if (gx > INT32_MAX || gy > 65535) return fail(NIMBLE_ERR_INVALID_ARG, "transpose extent too large");
-  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), block(32, 8);
-  if (elem_size(dtype) == 4)
-    transpose_kernel<float><<<grid, block, 0, s>>>(static_cast<const float*>(src), R, C, ld_src,
-                                                   static_cast<float*>(dst), ld_dst);
-  else
-    transpose_kernel<uint16_t><<<grid, block, 0, s>>>(static_cast<const uint16_t*>(src), R, C, ld_src,
-                                                      static_cast<uint16_t*>(dst), ld_dst);
-  NIMBLE_CUDA_TRY(cudaGetLastError());
-  return NIMBLE_OK;
 }
 
 int launch_round(const float* src, float* dst, int64_t n, cudaStream_t s) {
@@ -753,29 +748,25 @@ FwdLayout fwd_layout(int64_t N, int64_t d, int64_t V, int dtype) {
   return L;
 }
 
-constexpr size_t kDefaultSlabBytes = size_t(1) << 30;
+constexpr size_t kDefaultSlabBytes = size_t(2) << 30;
 
+// Backward workspace: the G slab (N x slab columns), an fp32 dh accumulator
+// when the shard needs more than one slab, and (fp32) tf32-rounded operands.
 struct BwdLayout {
-  int64_t slab = 0, ldn = 0, ldv = 0, n_slabs = 0;
-  size_t g = 0, gt = 0, ht = 0, et = 0, dh = 0, hr = 0, er = 0, total = 0;
+  int64_t slab = 0, n_slabs = 0;
+  size_t g = 0, dh = 0, hr = 0, er = 0, total = 0;
 };
 BwdLayout bwd_layout(int64_t N, int64_t d, int64_t V, int dtype, size_t slab_bytes) {
   BwdLayout L;
   const int64_t es = elem_size(dtype);
   if (slab_bytes == 0) slab_bytes = kDefaultSlabBytes;
-  L.ldn = round_up(N, 64);
-  L.ldv = round_up(V, 64);
-  // G (N x slab) and G^T (slab x ldn) share the slab budget.
-  int64_t cols = static_cast<int64_t>(slab_bytes / (2 * es * std::max<int64_t>(L.ldn, 1)));
+  int64_t cols = static_cast<int64_t>(slab_bytes / (es * std::max<int64_t>(N, 1)));
   cols = std::max<int64_t>(kBN, cols / kBN * kBN);
   cols = std::min<int64_t>(cols, round_up(V, kBN));
   L.slab = cols;
   L.n_slabs = (V + cols - 1) / cols;
   size_t off = 0;
   L.g = off; off = align_up(off + es * N * cols);
-  L.gt = off; off = align_up(off + es * cols * L.ldn);
-  L.ht = off; off = align_up(off + es * d * L.ldn);
-  L.et = off; off = align_up(off + es * d * L.ldv);
   if (L.n_slabs > 1) { L.dh = off; off = align_up(off + sizeof(float) * N * d); }
   if (dtype == NIMBLE_DTYPE_F32) {
     L.hr = off; off = align_up(off + sizeof(float) * N * d);
@@ -922,12 +913,7 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
     E = er;
   }
   void* g = ws + L.g;
-  void* gt = ws + L.gt;
-  void* ht = ws + L.ht;
-  void* et = ws + L.et;
   float* dh_acc = L.n_slabs > 1 ? reinterpret_cast<float*>(ws + L.dh) : nullptr;
-  if (int rc = launch_transpose(dtype, h, n_tokens, d_model, d_model, ht, L.ldn, s)) return rc;
-  if (int rc = launch_transpose(dtype, E, v_local, d_model, d_model, et, L.ldv, s)) return rc;
 
   // G is stored scaled by 2^15 in fp16 so that softmax probabilities of order
   // 1/V stay in the normal range; the scale is undone in the dE / dh epilogue.
@@ -936,7 +922,7 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
     const int64_t c0 = sl * L.slab;
     const int64_t vc = std::min<int64_t>(L.slab, v_local - c0);
     const void* E_sl = static_cast<const uint8_t*>(E) + es * c0 * d_model;
-    // 1) recompute logits of the slab and write G, G^T.
+    // 1) recompute the slab's logits, write G [N x vc] (row pitch L.slab).
     EpiParams eg{};
     eg.labels = labels;
     eg.col_origin = v_offset + c0;
@@ -944,12 +930,11 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
     eg.lse = lse;
     eg.g = g;
     eg.ldg = L.slab;
-    eg.gt = gt;
-    eg.ldgt = L.ldn;
     eg.gscale = gscale;
     eg.status = status;
     if (int rc = gemm_dispatch<EPI_CE_GRAD>(dtype, h, d_model, E_sl, d_model, n_tokens, vc, d_model, eg, s)) return rc;
-    // 2) dE[c0:c0+vc] = G^T h  (K = tokens).
+    // 2) dE[c0:c0+vc] = G^T h: A = G read MN-major ([tokens x vc]), B = h
+    //    read MN-major ([tokens x d]); K = tokens.
     EpiParams ee{};
     ee.out = static_cast<uint8_t*>(grad_weights) + elem_size(grad_weights_dtype) * c0 * d_model;
     ee.ld_out = d_model;
@@ -959,8 +944,10 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
     ee.alpha_mult = 1.0f / gscale;
     ee.accum_out = accumulate_grad_weights ? 1 : 0;
     ee.status = status;
-    if (int rc = gemm_dispatch<EPI_STORE>(dtype, gt, L.ldn, ht, L.ldn, vc, d_model, n_tokens, ee, s)) return rc;
-    // 3) dh (+)= G E[c0:c0+vc]  (K = slab columns).
+    if (int rc = gemm_dispatch<EPI_STORE, true, true>(dtype, g, L.slab, h, d_model, vc, d_model, n_tokens, ee, s))
+      return rc;
+    // 3) dh (+)= G E[c0:c0+vc]: A = G K-major, B = E slab read MN-major
+    //    ([vc x d]); K = slab columns.
     EpiParams eh{};
     eh.status = status;
     const bool last = sl == L.n_slabs - 1;
@@ -978,8 +965,8 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
     eh.ld_out = d_model;
     eh.src = sl > 0 ? dh_acc : nullptr;
     eh.ld_src = d_model;
-    const void* et_sl = static_cast<const uint8_t*>(et) + es * c0;
-    if (int rc = gemm_dispatch<EPI_STORE>(dtype, g, L.slab, et_sl, L.ldv, n_tokens, d_model, vc, eh, s)) return rc;
+    if (int rc = gemm_dispatch<EPI_STORE, false, true>(dtype, g, L.slab, E_sl, d_model, n_tokens, d_model, vc, eh, s))
+      return rc;
   }
   return NIMBLE_OK;
 }

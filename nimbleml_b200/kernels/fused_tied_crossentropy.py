@@ -46,7 +46,7 @@ _TORCH_TO_NIMBLE = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bf
 # host sync) and raise on out-of-range labels — the reference's bounds-check
 # knob (NimbleML/kernels/embedding_scatter.py:9-22) applied to this path.
 CHECK_BOUNDS = os.environ.get("NIMBLEML_CHECK_BOUNDS", "0") not in ("", "0", "false", "False")
-# Per-slab budget (bytes) for the backward's G / G^T tiles; 0 = library default.
+# Per-slab budget (bytes) for the backward's G tile; 0 = library default.
 SLAB_BYTES = int(os.environ.get("NIMBLEML_TIED_CE_SLAB_BYTES", "0"))
 
 
@@ -164,8 +164,8 @@ def shard_backward(grad_scale: torch.Tensor, h: torch.Tensor, w: torch.Tensor, l
                    accumulate: bool = False, slab_bytes: Optional[int] = None):
     """(grad_hidden partial over this shard, grad_weights of the shard).
 
-    ``slab_bytes`` bounds the vocab slab's G / G^T scratch (default: the
-    NIMBLEML_TIED_CE_SLAB_BYTES environment value, else the library's 1 GiB).
+    ``slab_bytes`` bounds the vocab slab's G scratch (default: the
+    NIMBLEML_TIED_CE_SLAB_BYTES environment value, else the library's 2 GiB).
     """
     n, d = h.shape
     v_local = w.shape[0]

@@ -106,7 +106,7 @@ def test_multi_slab_backward_matches_single_slab():
     h, e, y = orc.make_inputs(n, d, v, seed=9, unit_rms=True)
     one = run_path(h, e, y, torch.float16)
     # 256-column slabs: 9 slabs, dh accumulated in the fp32 scratch.
-    many = run_path(h, e, y, torch.float16, slab_bytes=2 * 2 * 384 * 256)
+    many = run_path(h, e, y, torch.float16, slab_bytes=2 * 384 * 256)
     assert one[0] == many[0]
     # dh: fp32 partial sums over slabs vs one fp32 accumulation, then fp16
     # output rounding; dE rows of each slab are computed identically.
