@@ -30,6 +30,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -49,6 +50,10 @@ constexpr int kBBytes = kBN * kBKBytes;  // 32 KiB
 constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kTmemCols = 2 * kBN;  // two accumulators
 constexpr int kSmemBytes = kStages * (kABytes + kBBytes) + 1024 /*align*/ + 256 /*barriers*/;
+// CTA-pair mode (cta_group::2): each CTA holds 128 rows of A and 128 of the
+// 256 B rows per stage (32 KiB), so the ring is 6 stages deep.
+constexpr int kStagesPair = 6;
+constexpr int kSmemBytesPair = kStagesPair * (kABytes + kBBytes / 2) + 1024 + 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
 enum Epi : int { EPI_CE_FWD = 0, EPI_CE_GRAD = 1, EPI_STORE = 2 };
@@ -159,17 +164,26 @@ __device__ __forceinline__ void store_out_elem(void* p, int64_t i, int dt, float
 // of tile i while the MMAs of tile i+1 proceed. kAMN / kBMN select an
 // MN-major A / B operand (the tensor map's inner dimension is then M / N and
 // the tile arrives as 128-byte-wide MN chunks of K rows).
-template <typename T, int EPI, bool kAMN, bool kBMN>
+//
+// kCG = 2 runs CTA pairs (clusters of 2): the pair computes a 256 x 256 tile
+// with tcgen05.mma.cta_group::2 issued by the even CTA; each CTA loads its own
+// 128 A rows and 128 of the B rows, its TMEM holds its 128 accumulator rows,
+// and its epilogue warps write them. Loads are never multicast.
+template <typename T, int EPI, bool kAMN, bool kBMN, int kCG>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
                   int N, int K, int group_m, EpiParams ep) {
+  constexpr int kS = kCG == 2 ? kStagesPair : kStages;   // ring depth
+  constexpr int kBRows = kBN / kCG;                       // B rows loaded per CTA
+  constexpr int kBBytesCta = kBRows * kBKBytes;
+  constexpr int kTileM = kBM * kCG;                       // accumulator rows per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + kStages * kABytes;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + kStages * kBBytes);
-  uint64_t* empty_bar = full_bar + kStages;
-  uint64_t* tfull_bar = empty_bar + kStages;
+  uint8_t* sB = smem + kS * kABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + kS * kBBytesCta);
+  uint64_t* empty_bar = full_bar + kS;
+  uint64_t* tfull_bar = empty_bar + kS;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
@@ -183,31 +197,33 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_tiles = (M + kBM - 1) / kBM;
+  const int m_tiles = (M + kTileM - 1) / kTileM;
   const int n_tiles = (N + kBN - 1) / kBN;
   const int tiles = m_tiles * n_tiles;
   const int k_blocks = (K + kBK - 1) / kBK;
+  const uint32_t rank = kCG == 2 ? ptx::cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit0 = blockIdx.x / kCG;       // this CTA's first tile
+  const int units = gridDim.x / kCG;        // tile stride
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kS; ++s) {
       ptx::mbar_init(&full_bar[s], 1);
       ptx::mbar_init(&empty_bar[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull_bar[a], 1);
-      ptx::mbar_init(&tempty_bar[a], 4);
+      ptx::mbar_init(&tempty_bar[a], 4 * kCG);
     }
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
   }
-  if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, kTmemCols);
-    ptx::tmem_relinquish();
-  }
+  if (warp == 1) ptx::tmem_alloc_cg<kCG>(tmem_slot, kTmemCols);
   ptx::tc_fence_before();
   __syncthreads();
+  if constexpr (kCG == 2) ptx::cluster_sync();  // peer barriers initialised
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -220,37 +236,44 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       uint32_t phase = 0;
       uint32_t issued = 0;  // bit s: stage s has a load outstanding-or-done
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      auto load = [&](void* dst, const CUtensorMap* m, int stg, int x, int y) {
+        if constexpr (kCG == 2)
+          ptx::tma_load_2d_pair(dst, m, ptx::mapa_shared(&full_bar[stg], 0), x, y);
+        else
+          ptx::tma_load_2d(dst, m, &full_bar[stg], x, y);
+      };
+      for (int t = unit0; t < tiles && ok; t += units) {
         int mb, nb;
         tile_coords(t, m_tiles, n_tiles, group_m, mb, nb);
+        const int a_row0 = mb * kTileM + static_cast<int>(rank) * kBM;
+        const int b_row0 = nb * kBN + static_cast<int>(rank) * kBRows;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!ptx::mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) { ok = false; break; }
-          ptx::mbar_arrive_expect_tx(&full_bar[stage], kABytes + kBBytes);
+          // The even CTA's full barrier counts both CTAs' bytes.
+          if (leader) ptx::mbar_arrive_expect_tx(&full_bar[stage], kCG * (kABytes + kBBytesCta));
           if constexpr (kAMN) {
 #pragma unroll
             for (int j = 0; j < kBM / kBK; ++j)
-              ptx::tma_load_2d(sA + stage * kABytes + j * kBK * 128, &tmA, &full_bar[stage], mb * kBM + j * kBK,
-                               kb * kBK);
+              load(sA + stage * kABytes + j * kBK * 128, &tmA, stage, a_row0 + j * kBK, kb * kBK);
           } else {
-            ptx::tma_load_2d(sA + stage * kABytes, &tmA, &full_bar[stage], kb * kBK, mb * kBM);
+            load(sA + stage * kABytes, &tmA, stage, kb * kBK, a_row0);
           }
           if constexpr (kBMN) {
 #pragma unroll
-            for (int j = 0; j < kBN / kBK; ++j)
-              ptx::tma_load_2d(sB + stage * kBBytes + j * kBK * 128, &tmB, &full_bar[stage], nb * kBN + j * kBK,
-                               kb * kBK);
+            for (int j = 0; j < kBRows / kBK; ++j)
+              load(sB + stage * kBBytesCta + j * kBK * 128, &tmB, stage, b_row0 + j * kBK, kb * kBK);
           } else {
-            ptx::tma_load_2d(sB + stage * kBBytes, &tmB, &full_bar[stage], kb * kBK, nb * kBN);
+            load(sB + stage * kBBytesCta, &tmB, stage, kb * kBK, b_row0);
           }
           issued |= 1u << stage;
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
+          if (++stage == kS) { stage = 0; phase ^= 1; }
         }
       }
-      if (!ok) {
+      if (!ok && leader) {
         // Let every load already issued land before the CTA can exit: the
         // most recent phase of each stage is `phase` for stages below the
         // cursor and `phase ^ 1` at or above it.
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kS; ++s) {
           if (!(issued & (1u << s))) continue;
           const uint32_t par = (s < stage) ? phase : (phase ^ 1);
           const uint64_t t0 = ptx::globaltimer_ns();
@@ -260,9 +283,9 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       // ------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = ptx::idesc_f32acc(ElemInfo<T>::kFmt, kBM, kBN, kAMN, kBMN);
+      constexpr uint32_t idesc = ptx::idesc_f32acc(ElemInfo<T>::kFmt, kTileM, kBN, kAMN, kBMN);
       // Start-address step (16-byte units) per MMA along K: 32 bytes inside a
       // K-major swizzle row, or kUK rows of 128 bytes for an MN-major tile.
       constexpr uint64_t kAStep = kAMN ? kUK * 128 / 16 : 2;
@@ -271,7 +294,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+      for (int t = unit0; t < tiles && ok; t += units, ++it) {
         const int acc = it & 1;
         const uint32_t aphase = (it >> 1) & 1;
         if (!ptx::mbar_wait(&tempty_bar[acc], aphase ^ 1, abort_flag)) { ok = false; break; }
@@ -281,21 +304,29 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           if (!ptx::mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
           const uint32_t a_addr = ptx::smem_u32(sA + stage * kABytes);
-          const uint32_t b_addr = ptx::smem_u32(sB + stage * kBBytes);
+          const uint32_t b_addr = ptx::smem_u32(sB + stage * kBBytesCta);
           const uint64_t adesc = kAMN ? ptx::sdesc_mn_sw128(a_addr, kBK * 128, kTF32) : ptx::sdesc_k_sw128(a_addr);
           const uint64_t bdesc = kBMN ? ptx::sdesc_mn_sw128(b_addr, kBK * 128, kTF32) : ptx::sdesc_k_sw128(b_addr);
 #pragma unroll
-          for (int k = 0; k < kKSteps; ++k)
-            ptx::umma<kTF32>(d_tmem, adesc + kAStep * k, bdesc + kBStep * k, idesc, (kb | k) != 0 ? 1u : 0u);
-          ptx::umma_commit(&empty_bar[stage]);
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
+          for (int k = 0; k < kKSteps; ++k) {
+            if constexpr (kCG == 2)
+              ptx::umma_pair<kTF32>(d_tmem, adesc + kAStep * k, bdesc + kBStep * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              ptx::umma<kTF32>(d_tmem, adesc + kAStep * k, bdesc + kBStep * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          // Frees this stage in both CTAs once the MMAs have read it.
+          if constexpr (kCG == 2) ptx::umma_commit_pair(&empty_bar[stage], 0x3);
+          else ptx::umma_commit(&empty_bar[stage]);
+          if (++stage == kS) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        ptx::umma_commit(&tfull_bar[acc]);
+        if constexpr (kCG == 2) ptx::umma_commit_pair(&tfull_bar[acc], 0x3);
+        else ptx::umma_commit(&tfull_bar[acc]);
       }
       if (!ok) {
         // Drain: wait until every MMA issued so far has finished.
-        ptx::umma_commit(drain_bar);
+        if constexpr (kCG == 2) ptx::umma_commit_pair(drain_bar, 0x1);
+        else ptx::umma_commit(drain_bar);
         const uint64_t t0 = ptx::globaltimer_ns();
         while (!ptx::mbar_try_wait(drain_bar, 0) && ptx::globaltimer_ns() - t0 < ptx::kWaitLimitNs) {
         }
@@ -311,8 +342,17 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       const float den = ep.alpha_den ? *ep.alpha_den : 1.0f;
       alpha = (den != 0.0f) ? num / den * ep.alpha_mult : 0.0f;
     }
+    // TMEM of an accumulator is handed back to the MMA issuer (even CTA).
+    auto release = [&](int acc) {
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (kCG == 2) ptx::mbar_arrive_cluster(ptx::mapa_shared(&tempty_bar[acc], 0));
+        else ptx::mbar_arrive(&tempty_bar[acc]);
+      }
+    };
     int it = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+    for (int t = unit0; t < tiles; t += units, ++it) {
       int mb, nb;
       tile_coords(t, m_tiles, n_tiles, group_m, mb, nb);
       const int acc = it & 1;
@@ -322,7 +362,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       if (!ok) break;
       ptx::tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kBN;
-      const int64_t row = static_cast<int64_t>(mb) * kBM + row_t;
+      const int64_t row = static_cast<int64_t>(mb) * kTileM + static_cast<int64_t>(rank) * kBM + row_t;
       const bool row_ok = row < M;
       const int ncols = min(kBN, N - nb * kBN);
       const int64_t col0_tile = static_cast<int64_t>(nb) * kBN;
@@ -368,9 +408,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
               if (j == jt) tval = v[j];
           }
         }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+        release(acc);
         if (row_ok) {
           ep.part[static_cast<int64_t>(nb) * M + row] = make_float2(mrun, srun);
           if (tcol >= 0) ep.tgt[row] = tval;
@@ -401,9 +439,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           const int64_t col = col0_tile + c * 32;
           if (row_ok) store_row32<T>(g + row * ep.ldg + col, v);
         }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+        release(acc);
       } else {  // EPI_STORE
 #pragma unroll 1
         for (int c = 0; c < kBN / 32; ++c) {
@@ -486,20 +522,22 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             }
           }
         }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+        release(acc);
       }
     }
   }
 
   ptx::tc_fence_before();
   __syncthreads();
+  __syncwarp();
+  // Neither CTA of a pair may leave while the other can still touch its
+  // shared memory, barriers or TMEM.
+  if constexpr (kCG == 2) ptx::cluster_sync();
   if (threadIdx.x == 0 && *abort_flag && ep.status) atomicOr(ep.status, NIMBLE_STATUS_WAIT_TIMEOUT);
   if (warp == 1) {
     __syncwarp();
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, kTmemCols);
+    ptx::tmem_dealloc_cg<kCG>(tmem_base, kTmemCols);
   }
 }
 
@@ -663,6 +701,22 @@ int make_operand_map(CUtensorMap* map, const void* base, int dtype, bool mn_majo
   return NIMBLE_OK;
 }
 
+// GEMM tiling mode. One CTA per 128 x 256 tile by default; CTA pairs
+// (cta_group::2, 256 x 256 tiles) with NIMBLEML_TIED_CE_CTA_PAIRS=1. The pair
+// kernel keeps the tensor pipe busier per clock but draws more energy per
+// FLOP, so under the B200's 1 kW cap it runs at lower clocks and is slower
+// over a whole fwd+bwd step.
+const bool g_cta_pairs = [] {
+  const char* v = std::getenv("NIMBLEML_TIED_CE_CTA_PAIRS");
+  return v && v[0] == '1';
+}();
+// Token blocks per rasterisation group (NIMBLEML_TIED_CE_GROUP_M, default 16).
+const int g_group_m = [] {
+  const char* v = std::getenv("NIMBLEML_TIED_CE_GROUP_M");
+  const int g = v ? std::atoi(v) : 0;
+  return g > 0 ? g : 16;
+}();
+
 struct DevInfo {
   int sms = 0;
   int major = 0;
@@ -689,16 +743,38 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t 
   if (int rc = device_info(&di)) return rc;
   CUtensorMap ma, mb;
   if (int rc = make_operand_map(&ma, A, dtype, kAMN, K, M, lda, kBM)) return rc;
-  if (int rc = make_operand_map(&mb, B, dtype, kBMN, K, N, ldb, kBN)) return rc;
-  auto kern = tc_gemm_tn_kernel<T, EPI, kAMN, kBMN>;
-  NIMBLE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-  const int64_t m_tiles = (M + kBM - 1) / kBM, n_tiles = (N + kBN - 1) / kBN;
-  const int64_t tiles = m_tiles * n_tiles;
-  if (tiles > INT32_MAX) return fail(NIMBLE_ERR_INVALID_ARG, "too many tiles");
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, di.sms));
-  const int group_m = 8;
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, static_cast<int>(M), static_cast<int>(N),
-                                                static_cast<int>(K), group_m, ep);
+  if (int rc = make_operand_map(&mb, B, dtype, kBMN, K, N, ldb, g_cta_pairs ? kBN / 2 : kBN)) return rc;
+  const int group_m = g_group_m;
+  if (g_cta_pairs) {
+    // CTA pairs: 256 x 256 tiles, one cluster of 2 CTAs per SM pair.
+    auto kern = tc_gemm_tn_kernel<T, EPI, kAMN, kBMN, 2>;
+    NIMBLE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytesPair));
+    const int64_t tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
+    if (tiles > INT32_MAX) return fail(NIMBLE_ERR_INVALID_ARG, "too many tiles");
+    const int pairs = static_cast<int>(std::min<int64_t>(tiles, di.sms / 2));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytesPair;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    NIMBLE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, static_cast<int>(M), static_cast<int>(N),
+                                       static_cast<int>(K), group_m, ep));
+  } else {
+    auto kern = tc_gemm_tn_kernel<T, EPI, kAMN, kBMN, 1>;
+    NIMBLE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    if (tiles > INT32_MAX) return fail(NIMBLE_ERR_INVALID_ARG, "too many tiles");
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, di.sms));
+    kern<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, static_cast<int>(M), static_cast<int>(N),
+                                                  static_cast<int>(K), group_m, ep);
+  }
   NIMBLE_CUDA_TRY(cudaGetLastError());
   return NIMBLE_OK;
 }
