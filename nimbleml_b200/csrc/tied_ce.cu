@@ -725,6 +725,14 @@ struct DevInfo {
 int device_info(DevInfo* info) {
   int dev = 0;
   NIMBLE_CUDA_TRY(cudaGetDevice(&dev));
+  // cuTensorMapEncodeTiled is a driver call and needs a current context; a
+  // fresh host thread (e.g. torch's autograd worker) may not have one yet.
+  // cudaSetDevice makes the device's primary context current on this thread.
+  thread_local int ctx_dev = -1;
+  if (ctx_dev != dev) {
+    NIMBLE_CUDA_TRY(cudaSetDevice(dev));
+    ctx_dev = dev;
+  }
   NIMBLE_CUDA_TRY(cudaDeviceGetAttribute(&info->sms, cudaDevAttrMultiProcessorCount, dev));
   NIMBLE_CUDA_TRY(cudaDeviceGetAttribute(&info->major, cudaDevAttrComputeCapabilityMajor, dev));
   if (info->major != 10) return fail(NIMBLE_ERR_UNSUPPORTED, "requires a compute capability 10.x (B200) device");
