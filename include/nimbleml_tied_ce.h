@@ -135,6 +135,37 @@ NIMBLE_API int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
                             int accumulate_grad_weights, size_t slab_bytes, void* workspace,
                             size_t workspace_bytes, int* status, void* stream);
 
+/* Materialised tied-head logits for evaluation / generation:
+ *   logits[i, :] = hidden_row_i . E^T   (fp32 accumulate, f16 / bf16 inputs)
+ * where hidden_row_i starts hidden_row_pitch elements after row i-1, so
+ * passing (base + (S-1)*d, pitch S*d, n_rows = B) gives the last-position
+ * logits of each of B sequences of length S without a gather copy.
+ * Row i of logits starts logits_row_pitch elements after row i-1 (pitch x
+ * element size a multiple of 16 bytes; pad odd vocabularies). Only f16 / bf16
+ * compute. Replaces the GEMM of GPT._tied_logits
+ * (NimbleML/models/gpt.py:139-181) used by GPT.forward and generate
+ * (NimbleML/models/generate.py:62-119). */
+NIMBLE_API int nimble_tied_logits_forward(const void* hidden, int64_t hidden_row_pitch,
+                                          const void* weights, int64_t n_rows, int64_t d_model,
+                                          int64_t vocab, int dtype, void* logits,
+                                          int64_t logits_row_pitch, int logits_dtype, void* stream);
+
+/* Backward of the tied-head logits (NimbleML/models/gpt.py:165-178):
+ *   grad_hidden  = grad_logits . E          (skipped if grad_hidden is NULL)
+ *   grad_weights = grad_logits^T . hidden   (added to grad_weights when
+ *                                            accumulate_grad_weights != 0;
+ *                                            skipped if NULL)
+ * grad_logits (n_rows x vocab, rows grad_logits_row_pitch elements apart,
+ * pitch x element size a multiple of 16 bytes) and hidden (n_rows x d,
+ * contiguous) are in the compute dtype. */
+NIMBLE_API int nimble_tied_logits_backward(const void* grad_logits, int64_t grad_logits_row_pitch,
+                                           const void* hidden,
+                                           const void* weights, int64_t n_rows, int64_t d_model,
+                                           int64_t vocab, int dtype, void* grad_hidden,
+                                           int grad_hidden_dtype, void* grad_weights,
+                                           int grad_weights_dtype, int accumulate_grad_weights,
+                                           void* stream);
+
 /* Allocation-free variant of nimble_tied_ce_forward; no counterpart in the
  * reference. For callers that cannot allocate device memory (a runtime whose
  * GPU memory belongs to another framework's pool, or a binding that may only

@@ -1055,6 +1055,89 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
   return NIMBLE_OK;
 }
 
+// ======================================================== tied LM-head logits
+// Materialised logits of the tied head for evaluation and generation
+// (the reference's GPT.forward / _tied_logits), on the same tcgen05 GEMM with
+// the plain store epilogue.
+
+extern "C" int nimble_tied_logits_forward(const void* hidden, int64_t hidden_row_pitch, const void* weights,
+                                          int64_t n_rows, int64_t d_model, int64_t vocab, int dtype,
+                                          void* logits, int64_t logits_row_pitch, int logits_dtype,
+                                          void* stream) {
+  if (int rc = check_common(hidden, weights, reinterpret_cast<const int64_t*>(weights), n_rows, d_model, vocab,
+                            dtype))
+    return rc;
+  if (n_rows == 0) return NIMBLE_OK;
+  if (!logits) return fail(NIMBLE_ERR_INVALID_ARG, "null logits pointer");
+  if (logits_dtype != NIMBLE_DTYPE_F32 && logits_dtype != NIMBLE_DTYPE_F16 && logits_dtype != NIMBLE_DTYPE_BF16)
+    return fail(NIMBLE_ERR_INVALID_ARG, "bad logits dtype");
+  if (hidden_row_pitch < d_model) return fail(NIMBLE_ERR_INVALID_ARG, "hidden_row_pitch must be >= d_model");
+  if (logits_row_pitch < vocab) return fail(NIMBLE_ERR_INVALID_ARG, "logits_row_pitch must be >= vocab");
+  if ((reinterpret_cast<uintptr_t>(logits) & 15) || (logits_row_pitch * elem_size(logits_dtype)) % 16)
+    return fail(NIMBLE_ERR_INVALID_ARG, "logits must be 16-byte aligned with a row pitch of a multiple of 16 bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == NIMBLE_DTYPE_F32)
+    return fail(NIMBLE_ERR_INVALID_ARG, "tied logits support f16 / bf16 compute");
+  EpiParams ep{};
+  ep.out = logits;
+  ep.ld_out = logits_row_pitch;
+  ep.out_dtype = logits_dtype;
+  ep.alpha_mult = 1.0f;
+  return gemm_dispatch<EPI_STORE>(dtype, hidden, hidden_row_pitch, weights, d_model, n_rows, vocab, d_model, ep, s);
+}
+
+extern "C" int nimble_tied_logits_backward(const void* grad_logits, int64_t grad_logits_row_pitch,
+                                           const void* hidden, const void* weights,
+                                           int64_t n_rows, int64_t d_model, int64_t vocab, int dtype,
+                                           void* grad_hidden, int grad_hidden_dtype, void* grad_weights,
+                                           int grad_weights_dtype, int accumulate_grad_weights, void* stream) {
+  if (int rc = check_common(hidden, weights, reinterpret_cast<const int64_t*>(weights), n_rows, d_model, vocab,
+                            dtype))
+    return rc;
+  if (dtype == NIMBLE_DTYPE_F32)
+    return fail(NIMBLE_ERR_INVALID_ARG, "tied logits support f16 / bf16 compute");
+  if (n_rows > 0 && !grad_logits) return fail(NIMBLE_ERR_INVALID_ARG, "null grad_logits");
+  if (grad_logits_row_pitch < vocab) return fail(NIMBLE_ERR_INVALID_ARG, "grad_logits_row_pitch must be >= vocab");
+  for (int dt : {grad_hidden_dtype, grad_weights_dtype})
+    if (dt != NIMBLE_DTYPE_F32 && dt != NIMBLE_DTYPE_F16 && dt != NIMBLE_DTYPE_BF16)
+      return fail(NIMBLE_ERR_INVALID_ARG, "bad output dtype");
+  if ((grad_hidden && (reinterpret_cast<uintptr_t>(grad_hidden) & 15)) ||
+      (grad_weights && (reinterpret_cast<uintptr_t>(grad_weights) & 15)))
+    return fail(NIMBLE_ERR_INVALID_ARG, "gradient outputs must be 16-byte aligned");
+  if ((d_model * elem_size(grad_hidden_dtype)) % 16 || (d_model * elem_size(grad_weights_dtype)) % 16)
+    return fail(NIMBLE_ERR_INVALID_ARG, "d_model * output element size must be a multiple of 16 bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (grad_weights && n_rows == 0) {
+    if (!accumulate_grad_weights)
+      NIMBLE_CUDA_TRY(cudaMemsetAsync(grad_weights, 0, elem_size(grad_weights_dtype) * vocab * d_model, s));
+    return NIMBLE_OK;
+  }
+  if (grad_hidden) {
+    // grad_hidden = grad_logits . E: A = grad_logits K-major, B = E MN-major.
+    EpiParams eh{};
+    eh.out = grad_hidden;
+    eh.ld_out = d_model;
+    eh.out_dtype = grad_hidden_dtype;
+    eh.alpha_mult = 1.0f;
+    if (int rc = gemm_dispatch<EPI_STORE, false, true>(dtype, grad_logits, grad_logits_row_pitch, weights, d_model, n_rows, d_model,
+                                                       vocab, eh, s))
+      return rc;
+  }
+  if (grad_weights) {
+    // grad_weights (+)= grad_logits^T . hidden: both operands MN-major.
+    EpiParams ew{};
+    ew.out = grad_weights;
+    ew.ld_out = d_model;
+    ew.out_dtype = grad_weights_dtype;
+    ew.alpha_mult = 1.0f;
+    ew.accum_out = accumulate_grad_weights ? 1 : 0;
+    if (int rc = gemm_dispatch<EPI_STORE, true, true>(dtype, grad_logits, grad_logits_row_pitch, hidden, d_model, vocab, d_model,
+                                                      n_rows, ew, s))
+      return rc;
+  }
+  return NIMBLE_OK;
+}
+
 // ============================================ allocation-free forward variant
 // For callers that cannot allocate device memory at all: e.g. a host runtime
 // whose GPU memory is owned by another framework's pool, or an embedding

@@ -131,6 +131,28 @@ def tiny_gpt_case(nb):
                            "de": np.asarray(et.grad).reshape(e.shape)}
 
 
+def tied_logits_case(nb):
+    """GPT._tied_logits forward and backward on the tiny GPT (config 1 sizes)."""
+    from NimbleML import GPT, Tensor
+
+    nb.set_dtype("float32")
+    random.seed(0)
+    np.random.seed(0)
+    m = GPT(vocab_size=256, d_model=64, num_heads=4, num_layers=2, max_seq_len=32, fused_blocks=True)
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((2, 8, 64), dtype=np.float32)
+    g = rng.standard_normal((2, 8, 256), dtype=np.float32)
+    xt = Tensor(x.ravel(), (2, 8, 64), requires_grad=True)
+    m.token_emb.weights.zero_grad(set_to_none=True)
+    out = m._tied_logits(xt)
+    out.backward(g.ravel())
+    e = np.asarray(m.token_emb.weights._view()).astype(np.float32)
+    return "tied_logits_c1", {"x": x, "e": e, "grad_out": g, "logits": np.asarray(out._view()),
+                              "dx": np.asarray(xt.grad).reshape(2, 8, 64),
+                              "de": np.asarray(m.token_emb.weights.grad).reshape(e.shape),
+                              "loss": 0.0}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -138,6 +160,7 @@ def main():
     nb = _import_reference(Path(args.ref))
     cases = [
         tiny_gpt_case(nb),
+        tied_logits_case(nb),
         kernel_case(nb, "small_f32", 96, 64, 1000, 11, "float32"),
         kernel_case(nb, "small_f64", 96, 64, 1000, 11, "float64"),
         kernel_case(nb, "ragged_f32", 77, 40, 257, 12, "float32", force_edges=True),

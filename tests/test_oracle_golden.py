@@ -99,3 +99,11 @@ def test_sharded_combine_equals_full(p):
     assert abs(loss - l64) < 1e-12 * l64
     assert np.allclose(m, mx) and np.allclose(s, se, rtol=1e-12)
     assert nv == int(np.sum(y != -1))
+
+
+def test_tied_logits_head_matches_reference():
+    g = load("tied_logits_c1")
+    logits = orc.tied_logits_forward(g["x"], g["e"])
+    dx, de = orc.tied_logits_backward(g["grad_out"], g["x"], g["e"])
+    assert rel(logits, g["logits"]) < 1e-6
+    assert rel(dx, g["dx"]) < 1e-6 and rel(de, g["de"]) < 1e-6
