@@ -166,6 +166,94 @@ NIMBLE_API int nimble_tied_logits_backward(const void* grad_logits, int64_t grad
                                            int grad_weights_dtype, int accumulate_grad_weights,
                                            void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Row kernels around the head (HBM-bound, one read / write per element).
+ * ------------------------------------------------------------------------- */
+
+/* Cross-entropy over logits that already exist: the untied
+ * CrossEntropyLoss.forward (NimbleML/losses/cross_entropy.py:31-107) with
+ * fused_crossentropy_forward (NimbleML/kernels/fused_crossentropy.py:14-30).
+ * logits: n_rows x n_classes, rows row_pitch elements apart. Writes the row
+ * max, sum-exp and label logit (n_rows each), then lse, the mean loss over
+ * rows whose label != ignore_index, and that row count, exactly as
+ * nimble_tied_ce_combine does for one shard. */
+NIMBLE_API int nimble_ce_logits_forward(const void* logits, int64_t row_pitch, const int64_t* labels,
+                                        int64_t n_rows, int64_t n_classes, int dtype,
+                                        int64_t ignore_index, float* out_max, float* out_sumexp,
+                                        float* out_target, float* out_lse, float* out_loss,
+                                        float* out_valid_count, int* status, void* stream);
+
+/* grad_logits = (softmax - onehot) * grad_scale / n_valid, ignored rows zero
+ * (NimbleML/kernels/fused_crossentropy.py:33-50 and the row scatter of
+ * NimbleML/losses/_ce_prepare.py:72-78). grad_scale / valid_count are device
+ * scalars; lse comes from nimble_ce_logits_forward. */
+NIMBLE_API int nimble_ce_logits_backward(const float* grad_scale, const float* valid_count,
+                                         const void* logits, int64_t row_pitch, const int64_t* labels,
+                                         const float* lse, int64_t n_rows, int64_t n_classes, int dtype,
+                                         int64_t ignore_index, void* grad_logits,
+                                         int64_t grad_row_pitch, void* stream);
+
+/* Sampled softmax cross-entropy (NimbleML/kernels/sampled_softmax.py:66-98,
+ * NimbleML/losses/sampled_cross_entropy.py:21-119): softmax over the
+ * n_candidates classes of each row, candidates[i, 0] being the true class;
+ * rows whose label equals ignore_index are left out of the mean. */
+NIMBLE_API int nimble_sampled_ce_forward(const void* logits, int64_t row_pitch, const int64_t* candidates,
+                                         const int64_t* labels, int64_t n_rows, int64_t n_classes,
+                                         int64_t n_candidates, int dtype, int64_t ignore_index,
+                                         float* out_max, float* out_sumexp, float* out_target,
+                                         float* out_lse, float* out_loss, float* out_valid_count,
+                                         int* status, void* stream);
+
+/* Gradient of the sampled loss w.r.t. the full logits: zero everywhere except
+ * the candidate columns, where repeated candidates add up in order. */
+NIMBLE_API int nimble_sampled_ce_backward(const float* grad_scale, const float* valid_count,
+                                          const void* logits, int64_t row_pitch,
+                                          const int64_t* candidates, const int64_t* labels,
+                                          const float* lse, int64_t n_rows, int64_t n_classes,
+                                          int64_t n_candidates, int dtype, int64_t ignore_index,
+                                          void* grad_logits, int64_t grad_row_pitch, void* stream);
+
+/* RMSNorm over the last dimension (d_model <= 8192), the norm that produces
+ * the head's input: y = x / sqrt(mean(x^2) + eps) * gamma, with per-row
+ * mean(x^2) and rms saved for backward (NimbleML/layers/rms_norm.py:25-90,
+ * NimbleML/kernels/fused_rmsnorm.py:130-158). fp32 statistics. */
+NIMBLE_API int nimble_rmsnorm_forward(const void* x, const void* gamma, int64_t n_rows, int64_t d_model,
+                                      float eps, int dtype, void* y, float* out_ms, float* out_rms,
+                                      void* stream);
+
+/* Bytes of workspace nimble_rmsnorm_backward needs (per-block grad_gamma
+ * partial sums, reduced in a fixed order so the result is deterministic). */
+NIMBLE_API int nimble_rmsnorm_backward_workspace_size(int64_t n_rows, int64_t d_model, size_t* bytes);
+
+/* RMSNorm backward (NimbleML/kernels/fused_rmsnorm.py:161-217): grad_x in the
+ * compute dtype and grad_gamma in fp32 (added to grad_gamma when
+ * accumulate_grad_gamma != 0). */
+NIMBLE_API int nimble_rmsnorm_backward(const void* grad, const void* x, const void* gamma, const float* ms,
+                                       const float* rms, int64_t n_rows, int64_t d_model, float eps,
+                                       int dtype, void* grad_x, float* grad_gamma,
+                                       int accumulate_grad_gamma, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
+/* grad_weights[ids[i], :] += grad_out[i, :] into an fp32 (vocab x d) grad —
+ * the input-embedding share of the tied matrix's grad
+ * (NimbleML/kernels/embedding_scatter.py:39-81). Uses fp32 atomics, so the
+ * summation order of repeated ids is not fixed. Out-of-range ids are skipped
+ * and set NIMBLE_STATUS_BAD_LABEL. */
+NIMBLE_API int nimble_embedding_scatter_add(float* grad_weights, const int64_t* ids, const void* grad_out,
+                                            int64_t n_rows, int64_t vocab, int64_t d_model,
+                                            int grad_out_dtype, int* status, void* stream);
+
+/* One AdamW step over n fp32 master weights (NimbleML/optimizers/adam.py:20-43,
+ * the fused update used for each parameter, e.g. a vocab shard of E):
+ *   m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2;
+ *   w = w (1 - lr wd) - lr (m / bc1) / (sqrt(v / bc2) + eps)
+ * optionally also writing w to weights_copy in weights_copy_dtype. */
+NIMBLE_API int nimble_adamw_step(float* weights, const void* grad, int grad_dtype, float* exp_avg,
+                                 float* exp_avg_sq, int64_t n, float lr, float beta1, float beta2,
+                                 float bias_correction1, float bias_correction2, float eps,
+                                 float weight_decay, void* weights_copy, int weights_copy_dtype,
+                                 void* stream);
+
 /* Allocation-free variant of nimble_tied_ce_forward; no counterpart in the
  * reference. For callers that cannot allocate device memory (a runtime whose
  * GPU memory belongs to another framework's pool, or a binding that may only

@@ -59,6 +59,34 @@ SIGNATURES = {
         _c_int,
         [_c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_int, _c_vp, _c_int,
          _c_int, _c_vp]),
+    "nimble_ce_logits_forward": (
+        _c_int,
+        [_c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_int, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
+         _c_vp, _c_vp, _c_vp]),
+    "nimble_ce_logits_backward": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_i64, _c_vp, _c_i64,
+         _c_vp]),
+    "nimble_sampled_ce_forward": (
+        _c_int,
+        [_c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_i64, _c_vp, _c_vp, _c_vp,
+         _c_vp, _c_vp, _c_vp, _c_vp, _c_vp]),
+    "nimble_sampled_ce_backward": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_i64,
+         _c_vp, _c_i64, _c_vp]),
+    "nimble_rmsnorm_forward": (
+        _c_int, [_c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_float, _c_int, _c_vp, _c_vp, _c_vp, _c_vp]),
+    "nimble_rmsnorm_backward_workspace_size": (_c_int, [_c_i64, _c_i64, ctypes.POINTER(_c_size)]),
+    "nimble_rmsnorm_backward": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_float, _c_int, _c_vp, _c_vp,
+         _c_int, _c_vp, _c_size, _c_vp]),
+    "nimble_embedding_scatter_add": (
+        _c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
+    "nimble_adamw_step": (
+        _c_int,
+        [_c_vp, _c_vp, _c_int, _c_vp, _c_vp, _c_i64] + [ctypes.c_float] * 7 + [_c_vp, _c_int, _c_vp]),
     "nimble_tied_ce_backward": (
         _c_int,
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
@@ -99,6 +127,11 @@ class NativeLibrary:
         out = _c_size(0)
         self.call("nimble_tied_ce_backward_workspace_size", n, d, v_local, dtype, slab_bytes,
                   ctypes.byref(out))
+        return out.value
+
+    def rmsnorm_backward_workspace_size(self, n, d) -> int:
+        out = _c_size(0)
+        self.call("nimble_rmsnorm_backward_workspace_size", n, d, ctypes.byref(out))
         return out.value
 
 

@@ -18,8 +18,8 @@ REPO_DIR = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libnimbleml_tied_ce.so"
-SOURCES = [CSRC / "tied_ce.cu"]
-HEADERS = [CSRC / "sm100_ptx.cuh", REPO_DIR / "include" / "nimbleml_tied_ce.h"]
+SOURCES = [CSRC / "tied_ce.cu", CSRC / "rowwise.cu"]
+HEADERS = [CSRC / "sm100_ptx.cuh", CSRC / "common.cuh", REPO_DIR / "include" / "nimbleml_tied_ce.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

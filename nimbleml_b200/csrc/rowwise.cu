@@ -1,0 +1,551 @@
+// rowwise.cu — HBM-bound row kernels around the tied head (sm_100a).
+//
+// These are the steps either side of the fused tied cross-entropy:
+//   * cross-entropy over logits that already exist (the untied
+//     CrossEntropyLoss.forward and the sampled-softmax loss), reusing the
+//     shard-combine of the tied path for lse and the loss;
+//   * RMSNorm forward / backward, the norm that produces the head's input;
+//   * the embedding scatter-add that shares the tied matrix's grad, and the
+//     AdamW update of that matrix.
+// Each kernel reads and writes every element once; the roofline is HBM.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <string>
+
+#include "common.cuh"
+#include "nimbleml_tied_ce.h"
+
+namespace nimble {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Running (max, sum of exp(x - max)) with one exp per element: the sum is
+// rescaled only when the maximum grows.
+struct OnlineLse {
+  float m = -INFINITY, s = 0.0f;
+  __device__ __forceinline__ void add(float v) {
+    const float d = v - m;
+    if (d > 0.0f) {
+      s = s * ex2(-d * kLog2e) + 1.0f;
+      m = v;
+    } else {
+      s += ex2(d * kLog2e);
+    }
+  }
+  __device__ __forceinline__ void merge(float m2, float s2) {
+    if (m2 == -INFINITY) return;
+    if (m == -INFINITY) { m = m2; s = s2; return; }
+    const float mn = fmaxf(m, m2);
+    s = s * ex2((m - mn) * kLog2e) + s2 * ex2((m2 - mn) * kLog2e);
+    m = mn;
+  }
+};
+
+// One warp per row of a [N x V] logits matrix (row pitch ld): the row's
+// max, sum-exp and the label's logit (0 when the label is outside [0, V)).
+template <typename T>
+__global__ void ce_rows_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restrict__ labels, int64_t N,
+                               int64_t V, float* __restrict__ out_max, float* __restrict__ out_sum,
+                               float* __restrict__ out_tgt) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= N) return;
+  const T* r = x + row * ld;
+  OnlineLse acc;
+  constexpr int kVec = 16 / sizeof(T);
+  int64_t j0 = 0;
+  if ((reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+    const int64_t nvec = V / kVec;
+    const uint4* r4 = reinterpret_cast<const uint4*>(r);
+    for (int64_t q = lane; q < nvec; q += 32) {
+      const uint4 u = __ldg(r4 + q);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int k = 0; k < kVec; ++k) acc.add(to_f<T>(e[k]));
+    }
+    j0 = nvec * kVec;
+  }
+  for (int64_t j = j0 + lane; j < V; j += 32) acc.add(to_f<T>(r[j]));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, acc.m, off);
+    const float s2 = __shfl_xor_sync(0xffffffffu, acc.s, off);
+    acc.merge(m2, s2);
+  }
+  if (lane == 0) {
+    out_max[row] = acc.m;
+    out_sum[row] = acc.s;
+    const int64_t lab = labels[row];
+    out_tgt[row] = (lab >= 0 && lab < V) ? to_f<T>(r[lab]) : 0.0f;
+  }
+}
+
+// grad[i, j] = (exp(x_ij - lse_i) - [j == y_i]) * grad_scale / n_valid, rows
+// with y_i == ignore_index all zero. One warp per row.
+template <typename T>
+__global__ void ce_rows_grad_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restrict__ labels,
+                                    const float* __restrict__ lse, int64_t N, int64_t V, int64_t ignore_index,
+                                    const float* __restrict__ grad_scale, const float* __restrict__ valid_count,
+                                    T* __restrict__ g, int64_t ldg) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= N) return;
+  const float nv = *valid_count;
+  const int64_t lab = labels[row];
+  const bool live = lab != ignore_index && lab >= 0 && lab < V && nv > 0.0f;
+  const float scale = live ? *grad_scale / nv : 0.0f;
+  const float l2 = live ? lse[row] * kLog2e : 0.0f;
+  const T* r = x + row * ld;
+  T* o = g + row * ldg;
+  constexpr int kVec = 16 / sizeof(T);
+  int64_t j0 = 0;
+  if ((reinterpret_cast<uintptr_t>(r) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+    const int64_t nvec = V / kVec;
+    for (int64_t q = lane; q < nvec; q += 32) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(r) + q);
+      const T* e = reinterpret_cast<const T*>(&u);
+      uint4 w;
+      T* f = reinterpret_cast<T*>(&w);
+#pragma unroll
+      for (int k = 0; k < kVec; ++k) {
+        const int64_t j = q * kVec + k;
+        float p = live ? ex2(fmaf(to_f<T>(e[k]), kLog2e, -l2)) : 0.0f;
+        if (j == lab) p -= 1.0f;
+        f[k] = from_f<T>(p * scale);
+      }
+      reinterpret_cast<uint4*>(o)[q] = w;
+    }
+    j0 = nvec * kVec;
+  }
+  for (int64_t j = j0 + lane; j < V; j += 32) {
+    float p = live ? ex2(fmaf(to_f<T>(r[j]), kLog2e, -l2)) : 0.0f;
+    if (j == lab) p -= 1.0f;
+    o[j] = from_f<T>(p * scale);
+  }
+}
+
+// Sampled softmax, one thread per row over its C candidate classes
+// (candidate 0 is the true class).
+template <typename T>
+__global__ void sampled_rows_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restrict__ cand, int64_t N,
+                                    int64_t V, int64_t C, float* __restrict__ out_max, float* __restrict__ out_sum,
+                                    float* __restrict__ out_tgt, int* status) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= N) return;
+  OnlineLse acc;
+  float t = 0.0f;
+  bool bad = false;
+  for (int64_t c = 0; c < C; ++c) {
+    const int64_t k = cand[row * C + c];
+    if (k < 0 || k >= V) { bad = true; continue; }
+    const float v = to_f<T>(x[row * ld + k]);
+    if (c == 0) t = v;
+    acc.add(v);
+  }
+  if (bad && status) atomicOr(status, NIMBLE_STATUS_BAD_LABEL);
+  out_max[row] = acc.m;
+  out_sum[row] = acc.s;
+  out_tgt[row] = t;
+}
+
+template <typename T>
+__global__ void sampled_rows_grad_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restrict__ cand,
+                                         const int64_t* __restrict__ labels, const float* __restrict__ lse, int64_t N,
+                                         int64_t V, int64_t C, int64_t ignore_index,
+                                         const float* __restrict__ grad_scale, const float* __restrict__ valid_count,
+                                         T* __restrict__ g, int64_t ldg) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= N) return;
+  const float nv = *valid_count;
+  if (labels[row] == ignore_index || nv <= 0.0f) return;
+  const float scale = *grad_scale / nv;
+  const float l2 = lse[row] * kLog2e;
+  // One thread owns the row, so repeated candidates add up in a fixed order.
+  for (int64_t c = 0; c < C; ++c) {
+    const int64_t k = cand[row * C + c];
+    if (k < 0 || k >= V) continue;
+    float p = ex2(fmaf(to_f<T>(x[row * ld + k]), kLog2e, -l2));
+    if (c == 0) p -= 1.0f;
+    T* dst = g + row * ldg + k;
+    *dst = from_f<T>(to_f<T>(*dst) + p * scale);
+  }
+}
+
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) t += red[i];
+  return t;
+}
+
+// y = x / sqrt(mean(x^2) + eps) * gamma, one block per row (grid-stride).
+template <typename T, int KMAX>
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ gamma, int64_t N, int d, float eps,
+                   T* __restrict__ y, float* __restrict__ out_ms, float* __restrict__ out_rms) {
+  __shared__ float red[kNormThreads / 32];
+  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+    const T* xr = x + row * d;
+    float xv[KMAX];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      const int j = threadIdx.x + k * kNormThreads;
+      xv[k] = j < d ? to_f<T>(xr[j]) : 0.0f;
+      ss = fmaf(xv[k], xv[k], ss);
+    }
+    const float ms = block_sum(ss, red) / static_cast<float>(d);
+    const float rms = sqrtf(ms + eps);
+    const float inv = 1.0f / rms;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      const int j = threadIdx.x + k * kNormThreads;
+      if (j < d) y[row * d + j] = from_f<T>(xv[k] * inv * to_f<T>(gamma[j]));
+    }
+    if (threadIdx.x == 0) {
+      out_ms[row] = ms;
+      out_rms[row] = rms;
+    }
+  }
+}
+
+// grad_x = grad*gamma/rms + x * (2/d) * (-1/2) * (sum_j grad_j gamma_j x_j) * (ms+eps)^(-3/2)
+// and, per block, partial sums over its rows of grad * x / rms for grad_gamma.
+template <typename T, int KMAX>
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_bwd_kernel(const T* __restrict__ grad, const T* __restrict__ x, const T* __restrict__ gamma,
+                   const float* __restrict__ ms, const float* __restrict__ rms, int64_t N, int d, float eps,
+                   T* __restrict__ gx, float* __restrict__ partial) {
+  __shared__ float red[kNormThreads / 32];
+  float gg[KMAX], gm[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    const int j = threadIdx.x + k * kNormThreads;
+    gg[k] = 0.0f;
+    gm[k] = j < d ? to_f<T>(gamma[j]) : 0.0f;
+  }
+  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+    float gv[KMAX], xv[KMAX];
+    float dot = 0.0f;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      const int j = threadIdx.x + k * kNormThreads;
+      gv[k] = j < d ? to_f<T>(grad[row * d + j]) : 0.0f;
+      xv[k] = j < d ? to_f<T>(x[row * d + j]) : 0.0f;
+      dot = fmaf(gv[k] * gm[k], xv[k], dot);
+    }
+    dot = block_sum(dot, red);
+    const float inv = 1.0f / rms[row];
+    const float msv = ms[row] + eps;
+    const float coef = (2.0f / static_cast<float>(d)) * (-0.5f) * dot / (msv * sqrtf(msv));
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      const int j = threadIdx.x + k * kNormThreads;
+      if (j < d) gx[row * d + j] = from_f<T>(gv[k] * gm[k] * inv + xv[k] * coef);
+      gg[k] = fmaf(gv[k], xv[k] * inv, gg[k]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    const int j = threadIdx.x + k * kNormThreads;
+    if (j < d) partial[static_cast<int64_t>(blockIdx.x) * d + j] = gg[k];
+  }
+}
+
+// grad_gamma[j] (+)= sum over blocks b = 0..G-1 of partial[b, j], in order.
+__global__ void sum_partials_kernel(const float* __restrict__ partial, int G, int d, float* __restrict__ out,
+                                    int accumulate) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= d) return;
+  float s = 0.0f;
+  for (int b = 0; b < G; ++b) s += partial[static_cast<int64_t>(b) * d + j];
+  out[j] = accumulate ? out[j] + s : s;
+}
+
+template <typename T>
+__global__ void scatter_add_kernel(float* __restrict__ gw, const int64_t* __restrict__ ids,
+                                   const T* __restrict__ go, int64_t N, int64_t V, int d, int* status) {
+  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+    const int64_t id = ids[row];
+    if (id < 0 || id >= V) {
+      if (threadIdx.x == 0 && status) atomicOr(status, NIMBLE_STATUS_BAD_LABEL);
+      continue;
+    }
+    for (int j = threadIdx.x; j < d; j += blockDim.x) atomicAdd(gw + id * d + j, to_f<T>(go[row * d + j]));
+  }
+}
+
+template <typename G, typename P>
+__global__ void adamw_kernel(float* __restrict__ w, const G* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, int64_t n, float lr, float b1, float b2, float bc1, float bc2,
+                             float eps, float wd, P* __restrict__ copy) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float gi = to_f<G>(g[i]);
+    const float mn = b1 * m[i] + (1.0f - b1) * gi;
+    const float vn = b2 * v[i] + (1.0f - b2) * gi * gi;
+    const float upd = (mn / bc1) / (sqrtf(vn / bc2) + eps);
+    const float wn = w[i] * (1.0f - lr * wd) - lr * upd;
+    m[i] = mn;
+    v[i] = vn;
+    w[i] = wn;
+    if (copy) copy[i] = from_f<P>(wn);
+  }
+}
+
+int grid_for(int64_t items, int per_block) {
+  const int64_t b = (items + per_block - 1) / per_block;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(b, 148 * 32)));
+}
+
+int check_rows(const void* x, int64_t ld, int64_t N, int64_t V, int dtype) {
+  if (!valid_dtype(dtype)) return fail(NIMBLE_ERR_INVALID_ARG, "dtype must be NIMBLE_DTYPE_F32, F16 or BF16");
+  if (N < 0 || V <= 0 || ld < V) return fail(NIMBLE_ERR_INVALID_ARG, "need n_rows >= 0, n_classes > 0, row pitch >= n_classes");
+  if (N > 0 && !x) return fail(NIMBLE_ERR_INVALID_ARG, "null logits pointer");
+  return NIMBLE_OK;
+}
+
+#define NIMBLE_DISPATCH(dtype, T, ...)                                      \
+  switch (dtype) {                                                          \
+    case NIMBLE_DTYPE_F32: { using T = float; __VA_ARGS__; break; }         \
+    case NIMBLE_DTYPE_F16: { using T = __half; __VA_ARGS__; break; }        \
+    default: { using T = __nv_bfloat16; __VA_ARGS__; break; }               \
+  }
+
+}  // namespace
+}  // namespace nimble
+
+using namespace nimble;
+
+// ------------------------------------------------------- CE over given logits
+extern "C" int nimble_ce_logits_forward(const void* logits, int64_t row_pitch, const int64_t* labels, int64_t n_rows,
+                                        int64_t n_classes, int dtype, int64_t ignore_index, float* out_max,
+                                        float* out_sumexp, float* out_target, float* out_lse, float* out_loss,
+                                        float* out_valid_count, int* status, void* stream) {
+  if (int rc = check_rows(logits, row_pitch, n_rows, n_classes, dtype)) return rc;
+  if (n_rows > 0 && (!labels || !out_max || !out_sumexp || !out_target))
+    return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_rows > 0) {
+    const int rows_per_block = 8;
+    const unsigned grid = static_cast<unsigned>((n_rows + rows_per_block - 1) / rows_per_block);
+    NIMBLE_DISPATCH(dtype, T,
+                    ce_rows_kernel<T><<<grid, 32 * rows_per_block, 0, s>>>(
+                        static_cast<const T*>(logits), row_pitch, labels, n_rows, n_classes, out_max, out_sumexp,
+                        out_target));
+    NIMBLE_CUDA_TRY(cudaGetLastError());
+  }
+  return nimble_tied_ce_combine(out_max, out_sumexp, out_target, 1, labels, n_rows, n_classes, ignore_index,
+                                nullptr, nullptr, out_lse, out_loss, out_valid_count, status, stream);
+}
+
+extern "C" int nimble_ce_logits_backward(const float* grad_scale, const float* valid_count, const void* logits,
+                                         int64_t row_pitch, const int64_t* labels, const float* lse, int64_t n_rows,
+                                         int64_t n_classes, int dtype, int64_t ignore_index, void* grad_logits,
+                                         int64_t grad_row_pitch, void* stream) {
+  if (int rc = check_rows(logits, row_pitch, n_rows, n_classes, dtype)) return rc;
+  if (grad_row_pitch < n_classes) return fail(NIMBLE_ERR_INVALID_ARG, "grad row pitch < n_classes");
+  if (n_rows == 0) return NIMBLE_OK;
+  if (!grad_scale || !valid_count || !labels || !lse || !grad_logits)
+    return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rows_per_block = 8;
+  const unsigned grid = static_cast<unsigned>((n_rows + rows_per_block - 1) / rows_per_block);
+  NIMBLE_DISPATCH(dtype, T,
+                  ce_rows_grad_kernel<T><<<grid, 32 * rows_per_block, 0, s>>>(
+                      static_cast<const T*>(logits), row_pitch, labels, lse, n_rows, n_classes, ignore_index,
+                      grad_scale, valid_count, static_cast<T*>(grad_logits), grad_row_pitch));
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+// ------------------------------------------------------------ sampled softmax
+extern "C" int nimble_sampled_ce_forward(const void* logits, int64_t row_pitch, const int64_t* candidates,
+                                         const int64_t* labels, int64_t n_rows, int64_t n_classes,
+                                         int64_t n_candidates, int dtype, int64_t ignore_index, float* out_max,
+                                         float* out_sumexp, float* out_target, float* out_lse, float* out_loss,
+                                         float* out_valid_count, int* status, void* stream) {
+  if (int rc = check_rows(logits, row_pitch, n_rows, n_classes, dtype)) return rc;
+  if (n_candidates <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "n_candidates must be positive");
+  if (n_rows > 0 && (!candidates || !labels || !out_max || !out_sumexp || !out_target))
+    return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_rows > 0) {
+    const unsigned grid = static_cast<unsigned>((n_rows + 127) / 128);
+    NIMBLE_DISPATCH(dtype, T,
+                    sampled_rows_kernel<T><<<grid, 128, 0, s>>>(static_cast<const T*>(logits), row_pitch, candidates,
+                                                                n_rows, n_classes, n_candidates, out_max,
+                                                                out_sumexp, out_target, status));
+    NIMBLE_CUDA_TRY(cudaGetLastError());
+  }
+  return nimble_tied_ce_combine(out_max, out_sumexp, out_target, 1, labels, n_rows, n_classes, ignore_index,
+                                nullptr, nullptr, out_lse, out_loss, out_valid_count, status, stream);
+}
+
+extern "C" int nimble_sampled_ce_backward(const float* grad_scale, const float* valid_count, const void* logits,
+                                          int64_t row_pitch, const int64_t* candidates, const int64_t* labels,
+                                          const float* lse, int64_t n_rows, int64_t n_classes, int64_t n_candidates,
+                                          int dtype, int64_t ignore_index, void* grad_logits, int64_t grad_row_pitch,
+                                          void* stream) {
+  if (int rc = check_rows(logits, row_pitch, n_rows, n_classes, dtype)) return rc;
+  if (grad_row_pitch < n_classes || n_candidates <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "bad sizes");
+  if (n_rows == 0) return NIMBLE_OK;
+  if (!grad_scale || !valid_count || !candidates || !labels || !lse || !grad_logits)
+    return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t es = elem_size(dtype);
+  NIMBLE_CUDA_TRY(cudaMemset2DAsync(grad_logits, grad_row_pitch * es, 0, n_classes * es, n_rows, s));
+  const unsigned grid = static_cast<unsigned>((n_rows + 127) / 128);
+  NIMBLE_DISPATCH(dtype, T,
+                  sampled_rows_grad_kernel<T><<<grid, 128, 0, s>>>(
+                      static_cast<const T*>(logits), row_pitch, candidates, labels, lse, n_rows, n_classes,
+                      n_candidates, ignore_index, grad_scale, valid_count, static_cast<T*>(grad_logits),
+                      grad_row_pitch));
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+// -------------------------------------------------------------------- RMSNorm
+namespace {
+constexpr int kNormMaxD = 32 * kNormThreads;  // 8192
+int norm_grid(int64_t N) { return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(N, 2 * 148))); }
+}  // namespace
+
+extern "C" int nimble_rmsnorm_forward(const void* x, const void* gamma, int64_t n_rows, int64_t d_model, float eps,
+                                      int dtype, void* y, float* out_ms, float* out_rms, void* stream) {
+  if (!valid_dtype(dtype)) return fail(NIMBLE_ERR_INVALID_ARG, "bad dtype");
+  if (n_rows < 0 || d_model <= 0 || d_model > kNormMaxD)
+    return fail(NIMBLE_ERR_INVALID_ARG, "need n_rows >= 0 and 0 < d_model <= 8192");
+  if (n_rows == 0) return NIMBLE_OK;
+  if (!x || !gamma || !y || !out_ms || !out_rms) return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int d = static_cast<int>(d_model);
+  const int grid = norm_grid(n_rows);
+  NIMBLE_DISPATCH(dtype, T, {
+    const T* xt = static_cast<const T*>(x);
+    const T* gt = static_cast<const T*>(gamma);
+    T* yt = static_cast<T*>(y);
+    if (d <= 4 * kNormThreads)
+      rmsnorm_fwd_kernel<T, 4><<<grid, kNormThreads, 0, s>>>(xt, gt, n_rows, d, eps, yt, out_ms, out_rms);
+    else if (d <= 16 * kNormThreads)
+      rmsnorm_fwd_kernel<T, 16><<<grid, kNormThreads, 0, s>>>(xt, gt, n_rows, d, eps, yt, out_ms, out_rms);
+    else
+      rmsnorm_fwd_kernel<T, 32><<<grid, kNormThreads, 0, s>>>(xt, gt, n_rows, d, eps, yt, out_ms, out_rms);
+  });
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+extern "C" int nimble_rmsnorm_backward_workspace_size(int64_t n_rows, int64_t d_model, size_t* bytes) {
+  if (!bytes || n_rows < 0 || d_model <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "bad arguments");
+  *bytes = sizeof(float) * static_cast<size_t>(norm_grid(n_rows)) * static_cast<size_t>(d_model);
+  return NIMBLE_OK;
+}
+
+extern "C" int nimble_rmsnorm_backward(const void* grad, const void* x, const void* gamma, const float* ms,
+                                       const float* rms, int64_t n_rows, int64_t d_model, float eps, int dtype,
+                                       void* grad_x, float* grad_gamma, int accumulate_grad_gamma, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  if (!valid_dtype(dtype)) return fail(NIMBLE_ERR_INVALID_ARG, "bad dtype");
+  if (n_rows < 0 || d_model <= 0 || d_model > kNormMaxD)
+    return fail(NIMBLE_ERR_INVALID_ARG, "need n_rows >= 0 and 0 < d_model <= 8192");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int d = static_cast<int>(d_model);
+  if (n_rows == 0) {
+    if (grad_gamma && !accumulate_grad_gamma) NIMBLE_CUDA_TRY(cudaMemsetAsync(grad_gamma, 0, sizeof(float) * d, s));
+    return NIMBLE_OK;
+  }
+  if (!grad || !x || !gamma || !ms || !rms || !grad_x || !grad_gamma)
+    return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  const int grid = norm_grid(n_rows);
+  if (!workspace || workspace_bytes < sizeof(float) * static_cast<size_t>(grid) * d)
+    return fail(NIMBLE_ERR_WORKSPACE, "rmsnorm backward workspace too small");
+  float* partial = static_cast<float*>(workspace);
+  NIMBLE_DISPATCH(dtype, T, {
+    const T* gt = static_cast<const T*>(grad);
+    const T* xt = static_cast<const T*>(x);
+    const T* gm = static_cast<const T*>(gamma);
+    T* gxt = static_cast<T*>(grad_x);
+    if (d <= 4 * kNormThreads)
+      rmsnorm_bwd_kernel<T, 4><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
+    else if (d <= 16 * kNormThreads)
+      rmsnorm_bwd_kernel<T, 16><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
+    else
+      rmsnorm_bwd_kernel<T, 32><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
+  });
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  sum_partials_kernel<<<(d + 255) / 256, 256, 0, s>>>(partial, grid, d, grad_gamma, accumulate_grad_gamma);
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+// ------------------------------------------------ embedding grad and AdamW
+extern "C" int nimble_embedding_scatter_add(float* grad_weights, const int64_t* ids, const void* grad_out,
+                                            int64_t n_rows, int64_t vocab, int64_t d_model, int grad_out_dtype,
+                                            int* status, void* stream) {
+  if (!valid_dtype(grad_out_dtype)) return fail(NIMBLE_ERR_INVALID_ARG, "bad dtype");
+  if (n_rows < 0 || vocab <= 0 || d_model <= 0 || d_model > INT32_MAX) return fail(NIMBLE_ERR_INVALID_ARG, "bad sizes");
+  if (n_rows == 0) return NIMBLE_OK;
+  if (!grad_weights || !ids || !grad_out) return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = static_cast<int>(std::min<int64_t>(n_rows, 148 * 16));
+  const int threads = d_model >= 256 ? 256 : 128;
+  NIMBLE_DISPATCH(grad_out_dtype, T,
+                  scatter_add_kernel<T><<<grid, threads, 0, s>>>(grad_weights, ids, static_cast<const T*>(grad_out),
+                                                                 n_rows, vocab, static_cast<int>(d_model), status));
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}
+
+extern "C" int nimble_adamw_step(float* weights, const void* grad, int grad_dtype, float* exp_avg, float* exp_avg_sq,
+                                 int64_t n, float lr, float beta1, float beta2, float bias_correction1,
+                                 float bias_correction2, float eps, float weight_decay, void* weights_copy,
+                                 int weights_copy_dtype, void* stream) {
+  if (!valid_dtype(grad_dtype) || (weights_copy && !valid_dtype(weights_copy_dtype)))
+    return fail(NIMBLE_ERR_INVALID_ARG, "bad dtype");
+  if (n < 0) return fail(NIMBLE_ERR_INVALID_ARG, "bad size");
+  if (n == 0) return NIMBLE_OK;
+  if (!weights || !grad || !exp_avg || !exp_avg_sq) return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(n, 256);
+  const int cdt = weights_copy ? weights_copy_dtype : NIMBLE_DTYPE_F32;
+  NIMBLE_DISPATCH(grad_dtype, G, {
+    NIMBLE_DISPATCH(cdt, P,
+                    adamw_kernel<G, P><<<grid, 256, 0, s>>>(weights, static_cast<const G*>(grad), exp_avg,
+                                                            exp_avg_sq, n, lr, beta1, beta2, bias_correction1,
+                                                            bias_correction2, eps, weight_decay,
+                                                            static_cast<P*>(weights_copy)));
+  });
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  return NIMBLE_OK;
+}

@@ -36,6 +36,7 @@
 #include <string>
 
 #include "nimbleml_tied_ce.h"
+#include "common.cuh"
 #include "sm100_ptx.cuh"
 
 namespace nimble {
@@ -623,8 +624,6 @@ __global__ void round_tf32_kernel(const float* __restrict__ src, float* __restri
 }
 
 // ================================================================ host side
-namespace {
-
 thread_local std::string g_last_error;
 
 int fail(int code, const std::string& msg) {
@@ -632,12 +631,7 @@ int fail(int code, const std::string& msg) {
   return code;
 }
 
-#define NIMBLE_CUDA_TRY(expr)                                                             \
-  do {                                                                                    \
-    cudaError_t e_ = (expr);                                                              \
-    if (e_ != cudaSuccess)                                                                \
-      return fail(NIMBLE_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));   \
-  } while (0)
+namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -653,7 +647,6 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-int elem_size(int dtype) { return dtype == NIMBLE_DTYPE_F32 ? 4 : 2; }
 
 CUtensorMapDataType tmap_dtype(int dtype) {
   if (dtype == NIMBLE_DTYPE_F32) return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;

@@ -97,8 +97,82 @@ def tied_cross_entropy(hidden2d, weights, labels, ignore_index: Optional[int] = 
     return _TiedCrossEntropy.apply(hidden2d, weights, labels, ign, int(vocab_offset), int(vocab_size), group)
 
 
+def _flatten_logits(logits):
+    """(2-D view, out_shape) for 1-D / 2-D / 3-D logits (NimbleML/losses/_ce_prepare.py:9-29)."""
+    if logits.ndim == 1:
+        return logits.reshape(1, -1), logits.shape
+    if logits.ndim == 2:
+        return logits, logits.shape
+    if logits.ndim == 3:
+        return logits.reshape(-1, logits.shape[-1]), logits.shape
+    raise ValueError("Cross-entropy expects 1D, 2D, or 3D logits.")
+
+
+def _loss_dtype(compute_dtype):
+    """The reference coerces the loss to its compute dtype (Tensor([loss], ()),
+    NimbleML/utils/tensor.py:147-153); it has no bf16 (NumPy falls back to
+    fp16, np_backend.py:164-166), so a bf16 computation returns fp32."""
+    return torch.float32 if compute_dtype == torch.bfloat16 else compute_dtype
+
+
+def _row_pitch_ok(x2d):
+    return x2d.stride(-1) == 1 and (x2d.stride(0) * x2d.element_size()) % 16 == 0
+
+
+class _LogitsCrossEntropy(torch.autograd.Function):
+    """Cross-entropy over given logits (the untied head), HBM-bound row kernels."""
+
+    @staticmethod
+    def forward(ctx, x2d, labels, ignore_index):
+        from nimbleml_b200.kernels.fused_tied_crossentropy import _TORCH_TO_NIMBLE, _stream_ptr, native, status_word
+
+        if not _row_pitch_ok(x2d):
+            x2d = x2d.contiguous()
+        n, v = x2d.shape
+        dev = x2d.device
+        st = torch.empty((3, n), dtype=torch.float32, device=dev)
+        lse = torch.empty(n, dtype=torch.float32, device=dev)
+        sc = torch.empty(2, dtype=torch.float32, device=dev)
+        native.call("nimble_ce_logits_forward", x2d.data_ptr(), x2d.stride(0), labels.data_ptr(), n, v,
+                    _TORCH_TO_NIMBLE[x2d.dtype], ignore_index, st[0].data_ptr(), st[1].data_ptr(),
+                    st[2].data_ptr(), lse.data_ptr(), sc[0:1].data_ptr(), sc[1:2].data_ptr(),
+                    status_word(dev).data_ptr(), _stream_ptr(dev))
+        if CHECK_BOUNDS:
+            check_status(dev)
+        ctx.save_for_backward(x2d, labels, lse, sc[1:2])
+        ctx.ignore_index = ignore_index
+        return sc[0]
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        from nimbleml_b200.kernels.fused_tied_crossentropy import _TORCH_TO_NIMBLE, _stream_ptr, native
+
+        x2d, labels, lse, valid = ctx.saved_tensors
+        n, v = x2d.shape
+        gs = grad_out.reshape(1).float().contiguous()
+        g = torch.empty_like(x2d, memory_format=torch.contiguous_format)
+        native.call("nimble_ce_logits_backward", gs.data_ptr(), valid.data_ptr(), x2d.data_ptr(), x2d.stride(0),
+                    labels.data_ptr(), lse.data_ptr(), n, v, _TORCH_TO_NIMBLE[x2d.dtype], ctx.ignore_index,
+                    g.data_ptr(), g.stride(0), _stream_ptr(x2d.device))
+        return g, None, None
+
+
 class CrossEntropyLoss:
-    """Subset of NimbleML's ``CrossEntropyLoss`` that the tied head needs."""
+    """NimbleML's ``CrossEntropyLoss``: the fused tied head and CE over given logits."""
+
+    def forward(self, logits, labels, ignore_index=None):
+        """Mean cross-entropy of (classes,), (batch, classes) or (batch, seq, classes) logits.
+
+        Mirrors NimbleML/losses/cross_entropy.py:31-107 (ignored rows are
+        masked in the kernel; the loss is returned in the logits' dtype).
+        """
+        if not logits.is_cuda:
+            raise RuntimeError("CrossEntropyLoss on B200 needs CUDA tensors; there is no CPU path")
+        compute_dtype_of(logits)
+        x2d, _ = _flatten_logits(logits)
+        labels = as_label_indices(labels, batch_size=x2d.shape[0], device=logits.device)
+        ign = _NO_IGNORE if ignore_index is None else int(ignore_index)
+        return _LogitsCrossEntropy.apply(x2d, labels, ign).to(_loss_dtype(logits.dtype))
 
     def forward_tied(self, hidden, embedding_weights, labels, ignore_index=None):
         """Cross-entropy with tied ``hidden @ embedding_weights.T`` logits.
@@ -122,9 +196,10 @@ class CrossEntropyLoss:
             weights = weights.contiguous()
         label_indices = as_label_indices(labels, batch_size=row_count, device=hidden.device)
         loss = tied_cross_entropy(h2d, weights, label_indices, ignore_index)
-        return loss.to(hidden.dtype)
+        return loss.to(_loss_dtype(hidden.dtype))
 
-    __call__ = forward_tied
+    def __call__(self, logits, labels, ignore_index=None):
+        return self.forward(logits, labels, ignore_index=ignore_index)
 
 
 __all__ = ["CrossEntropyLoss", "tied_cross_entropy", "_as_cuda"]

@@ -153,6 +153,61 @@ def tied_logits_case(nb):
                               "loss": 0.0}
 
 
+def row_kernels_case(nb):
+    """Reference outputs for the row kernels around the head (fp32)."""
+    from NimbleML.kernels import (embedding_scatter_add, fused_rmsnorm_backward, fused_rmsnorm_forward,
+                                  sampled_softmax_backward, sampled_softmax_forward)
+    from NimbleML.losses.cross_entropy import CrossEntropyLoss
+    from NimbleML.utils.tensor import Tensor
+
+    nb.set_dtype("float32")
+    rng = np.random.default_rng(3)
+    out = {"loss": 0.0}
+    # Untied CE on (B, S, V) logits with ignore_index=-1.
+    logits = rng.standard_normal((3, 10, 77), dtype=np.float32) * 2
+    labels = rng.integers(0, 77, (3, 10))
+    labels[0, :3] = -1
+    lt = Tensor(logits.ravel(), logits.shape, requires_grad=True)
+    loss = CrossEntropyLoss().forward(lt, labels, ignore_index=-1)
+    loss.backward()
+    out.update(ce_logits=logits, ce_labels=labels, ce_loss=loss.item(),
+               ce_grad=np.asarray(lt.grad).reshape(logits.shape))
+    # Sampled softmax with fixed negatives (num_samples 7, V 50).
+    sl = rng.standard_normal((12, 50), dtype=np.float32)
+    sy = rng.integers(0, 50, 12)
+    neg = np.stack([rng.choice(np.delete(np.arange(50), sy[i]), 7, replace=False) for i in range(12)])
+    sloss, lg, cand, mx, se = sampled_softmax_forward(sl, sy, neg)
+    sgrad = sampled_softmax_backward(1.0, lg, cand, mx, se)
+    out.update(s_logits=sl, s_labels=sy, s_neg=neg, s_loss=sloss, s_grad=sgrad)
+    # RMSNorm forward / backward.
+    x = rng.standard_normal((9, 96), dtype=np.float32)
+    gamma = (1.0 + 0.1 * rng.standard_normal(96)).astype(np.float32)
+    y, xs, ms, rms = fused_rmsnorm_forward(x, gamma, 1e-5)
+    gy = rng.standard_normal((9, 96), dtype=np.float32)
+    gx, gg = fused_rmsnorm_backward(gy, xs, gamma, ms, rms, 1e-5)
+    out.update(n_x=x, n_gamma=gamma, n_y=y, n_ms=np.asarray(ms).ravel(), n_rms=np.asarray(rms).ravel(), n_gy=gy,
+               n_gx=gx, n_gg=gg)
+    # Embedding scatter-add with repeated ids.
+    gw = rng.standard_normal((40, 24), dtype=np.float32)
+    ids = rng.integers(0, 40, 64)
+    ids[:8] = 5
+    go = rng.standard_normal((64, 24), dtype=np.float32)
+    res = embedding_scatter_add(gw.copy(), ids, go)
+    out.update(e_gw=gw, e_ids=ids, e_go=go, e_out=np.asarray(res))
+    # Two AdamW steps on one fp32 parameter (reference optimizer, CPU path).
+    from NimbleML.optimizers import AdamW
+
+    w0 = rng.standard_normal(300).astype(np.float32)
+    grads = rng.standard_normal((2, 300)).astype(np.float32)
+    prm = Tensor(w0.copy(), (300,), requires_grad=True)
+    opt = AdamW([prm], learning_rate=1e-2, weight_decay=0.1)
+    for g in grads:
+        prm.grad = g.copy()
+        opt.step()
+    out.update(a_w0=w0, a_grads=grads, a_w2=np.asarray(prm.data).reshape(-1).copy())
+    return "row_kernels_f32", out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -161,6 +216,7 @@ def main():
     cases = [
         tiny_gpt_case(nb),
         tied_logits_case(nb),
+        row_kernels_case(nb),
         kernel_case(nb, "small_f32", 96, 64, 1000, 11, "float32"),
         kernel_case(nb, "small_f64", 96, 64, 1000, 11, "float64"),
         kernel_case(nb, "ragged_f32", 77, 40, 257, 12, "float32", force_edges=True),

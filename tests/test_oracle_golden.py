@@ -107,3 +107,24 @@ def test_tied_logits_head_matches_reference():
     dx, de = orc.tied_logits_backward(g["grad_out"], g["x"], g["e"])
     assert rel(logits, g["logits"]) < 1e-6
     assert rel(dx, g["dx"]) < 1e-6 and rel(de, g["de"]) < 1e-6
+
+
+def test_row_kernel_restatements_match_reference():
+    g = load("row_kernels_f32")
+    lg = g["ce_logits"].reshape(-1, g["ce_logits"].shape[-1])
+    loss, grad = orc.ce_logits_loss_and_grad(lg, g["ce_labels"], ignore_index=-1)
+    assert abs(loss - float(g["ce_loss"])) < 1e-6 * float(g["ce_loss"])
+    assert rel(grad, g["ce_grad"].reshape(lg.shape)) < 1e-6
+    sloss, sgrad, _ = orc.sampled_ce_loss_and_grad(g["s_logits"], g["s_labels"], g["s_neg"])
+    assert abs(sloss - float(g["s_loss"])) < 1e-6 * float(g["s_loss"])
+    assert rel(sgrad, g["s_grad"]) < 1e-6
+    y, ms, rms = orc.rmsnorm_forward(g["n_x"], g["n_gamma"])
+    assert rel(y, g["n_y"]) < 1e-6 and rel(rms.ravel(), g["n_rms"]) < 1e-6
+    gx, gg = orc.rmsnorm_backward(g["n_gy"], g["n_x"], g["n_gamma"], ms, rms)
+    assert rel(gx, g["n_gx"]) < 1e-5 and rel(gg, g["n_gg"]) < 1e-5
+    assert rel(orc.embedding_scatter_add(g["e_gw"], g["e_ids"], g["e_go"]), g["e_out"]) < 1e-6
+    w, m, v = g["a_w0"].astype(np.float64), 0.0, 0.0
+    for t, gr in enumerate(g["a_grads"], start=1):
+        w, m, v = orc.adamw_step(w, gr.astype(np.float64), m, v, 1e-2, 0.9, 0.999, 1 - 0.9 ** t,
+                                 1 - 0.999 ** t, 1e-8, 0.1)
+    assert rel(w, g["a_w2"]) < 1e-6
