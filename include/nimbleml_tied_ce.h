@@ -110,7 +110,8 @@ NIMBLE_API int nimble_tied_ce_combine(const float* shard_max, const float* shard
 
 /* Bytes of workspace nimble_tied_ce_backward needs. `slab_bytes` bounds the
  * per-slab gradient tiles (0 = library default, 2 GiB); the backward walks
- * the shard in vocab slabs whose G buffers fit that budget. */
+ * the shard in vocab slabs whose G buffers fit that budget, and in at least
+ * two slabs, so no buffer holds more than half of the shard's logits. */
 NIMBLE_API int nimble_tied_ce_backward_workspace_size(int64_t n_tokens, int64_t d_model, int64_t v_local,
                                            int dtype, size_t slab_bytes, size_t* bytes);
 

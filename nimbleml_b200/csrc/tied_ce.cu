@@ -839,7 +839,9 @@ BwdLayout bwd_layout(int64_t N, int64_t d, int64_t V, int dtype, size_t slab_byt
   if (slab_bytes == 0) slab_bytes = kDefaultSlabBytes;
   int64_t cols = static_cast<int64_t>(slab_bytes / (es * std::max<int64_t>(N, 1)));
   cols = std::max<int64_t>(kBN, cols / kBN * kBN);
-  cols = std::min<int64_t>(cols, round_up(V, kBN));
+  // At least two slabs: the G slab never holds more than half of the shard's
+  // N x V_local logits, however large the budget.
+  cols = std::min<int64_t>(cols, round_up((V + 1) / 2, kBN));
   L.slab = cols;
   L.n_slabs = (V + cols - 1) / cols;
   size_t off = 0;
