@@ -136,6 +136,13 @@ NIMBLE_API int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
                             int accumulate_grad_weights, size_t slab_bytes, void* workspace,
                             size_t workspace_bytes, int* status, void* stream);
 
+/* Diagnostic for the failure path (no counterpart in the reference, which has
+ * no device-side waits): launches one block whose bounded mbarrier wait —
+ * the same wait every pipeline stage of the GEMMs uses — has nothing to wait
+ * for. After limit_ns (at most 2 s) it gives up, ORs
+ * NIMBLE_STATUS_WAIT_TIMEOUT into *status and returns; no fault, no hang. */
+NIMBLE_API int nimble_tied_ce_probe_wait_timeout(uint64_t limit_ns, int* status, void* stream);
+
 /* Materialised tied-head logits for evaluation / generation:
  *   logits[i, :] = hidden_row_i . E^T   (fp32 accumulate, f16 / bf16 inputs)
  * where hidden_row_i starts hidden_row_pitch elements after row i-1, so

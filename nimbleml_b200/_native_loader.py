@@ -53,6 +53,7 @@ SIGNATURES = {
          _c_vp, _c_vp, _c_vp, _c_vp]),
     "nimble_tied_ce_backward_workspace_size": (
         _c_int, [_c_i64, _c_i64, _c_i64, _c_int, _c_size, ctypes.POINTER(_c_size)]),
+    "nimble_tied_ce_probe_wait_timeout": (_c_int, [ctypes.c_uint64, _c_vp, _c_vp]),
     "nimble_tied_logits_forward": (
         _c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_i64, _c_int, _c_vp]),
     "nimble_tied_logits_backward": (

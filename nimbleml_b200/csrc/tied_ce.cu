@@ -699,10 +699,19 @@ int make_operand_map(CUtensorMap* map, const void* base, int dtype, bool mn_majo
 // kernel keeps the tensor pipe busier per clock but draws more energy per
 // FLOP, so under the B200's 1 kW cap it runs at lower clocks and is slower
 // over a whole fwd+bwd step.
-const bool g_cta_pairs = [] {
+// The value is a bit mask over GEMM kinds: 1 forward, 2 recompute, 4 the
+// store GEMMs with an MN-major A (dE), 8 the store GEMMs with a K-major A (dh);
+// "1" alone keeps its historical meaning of all kinds.
+const int g_cta_pairs = [] {
   const char* v = std::getenv("NIMBLEML_TIED_CE_CTA_PAIRS");
-  return v && v[0] == '1';
+  if (!v) return 0;
+  const int m = std::atoi(v);
+  return m == 1 ? 15 : m;
 }();
+template <int EPI, bool kAMN>
+constexpr int gemm_kind_bit() {
+  return EPI == EPI_CE_FWD ? 1 : EPI == EPI_CE_GRAD ? 2 : kAMN ? 4 : 8;
+}
 // Token blocks per rasterisation group (NIMBLEML_TIED_CE_GROUP_M, default 16).
 const int g_group_m = [] {
   const char* v = std::getenv("NIMBLEML_TIED_CE_GROUP_M");
@@ -744,9 +753,10 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t 
   if (int rc = device_info(&di)) return rc;
   CUtensorMap ma, mb;
   if (int rc = make_operand_map(&ma, A, dtype, kAMN, K, M, lda, kBM)) return rc;
-  if (int rc = make_operand_map(&mb, B, dtype, kBMN, K, N, ldb, g_cta_pairs ? kBN / 2 : kBN)) return rc;
+  const bool pairs = (g_cta_pairs & gemm_kind_bit<EPI, kAMN>()) != 0;
+  if (int rc = make_operand_map(&mb, B, dtype, kBMN, K, N, ldb, pairs ? kBN / 2 : kBN)) return rc;
   const int group_m = g_group_m;
-  if (g_cta_pairs) {
+  if (pairs) {
     // CTA pairs: 256 x 256 tiles, one cluster of 2 CTAs per SM pair.
     auto kern = tc_gemm_tn_kernel<T, EPI, kAMN, kBMN, 2>;
     NIMBLE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytesPair));
@@ -1047,6 +1057,32 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
     if (int rc = gemm_dispatch<EPI_STORE, false, true>(dtype, g, L.slab, E_sl, d_model, n_tokens, d_model, vc, eh, s))
       return rc;
   }
+  return NIMBLE_OK;
+}
+
+// ================================================================ diagnostics
+// One block waits on an mbarrier that nothing will ever arrive on, through the
+// same bounded wait the GEMM pipeline uses; it must give up after limit_ns,
+// report NIMBLE_STATUS_WAIT_TIMEOUT and leave the context usable.
+__global__ void wait_timeout_probe_kernel(int* status, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = ptx::mbar_wait(&bar, 0, &abort_flag, limit_ns);
+  __syncthreads();
+  if (threadIdx.x == 0 && (!ok || abort_flag)) atomicOr(status, NIMBLE_STATUS_WAIT_TIMEOUT);
+}
+
+extern "C" int nimble_tied_ce_probe_wait_timeout(uint64_t limit_ns, int* status, void* stream) {
+  if (!status) return fail(NIMBLE_ERR_INVALID_ARG, "null status");
+  if (limit_ns == 0 || limit_ns > ptx::kWaitLimitNs) return fail(NIMBLE_ERR_INVALID_ARG, "limit_ns must be in (0, 2 s]");
+  wait_timeout_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, limit_ns);
+  NIMBLE_CUDA_TRY(cudaGetLastError());
   return NIMBLE_OK;
 }
 
