@@ -50,11 +50,15 @@ constexpr int kABytes = kBM * kBKBytes;  // 16 KiB
 constexpr int kBBytes = kBN * kBKBytes;  // 32 KiB
 constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kTmemCols = 2 * kBN;  // two accumulators
-constexpr int kSmemBytes = kStages * (kABytes + kBBytes) + 1024 /*align*/ + 256 /*barriers*/;
+// Staging for the G tile stores: per epilogue warp two 32 x 32 buffers of up
+// to 128-byte rows (4 KiB each).
+constexpr int kStoreBuf = 4096;
+constexpr int kStoreBytes = 4 * 2 * kStoreBuf;
+constexpr int kSmemBytes = kStages * (kABytes + kBBytes) + kStoreBytes + 1024 /*align*/ + 256 /*barriers*/;
 // CTA-pair mode (cta_group::2): each CTA holds 128 rows of A and 128 of the
 // 256 B rows per stage (32 KiB), so the ring is 6 stages deep.
 constexpr int kStagesPair = 6;
-constexpr int kSmemBytesPair = kStagesPair * (kABytes + kBBytes / 2) + 1024 + 256;
+constexpr int kSmemBytesPair = kStagesPair * (kABytes + kBBytes / 2) + kStoreBytes + 1024 + 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
 enum Epi : int { EPI_CE_FWD = 0, EPI_CE_GRAD = 1, EPI_STORE = 2 };
@@ -124,29 +128,6 @@ __device__ __forceinline__ uint32_t pack2(__nv_bfloat16 a, __nv_bfloat16 b) {
          (static_cast<uint32_t>(__bfloat16_as_ushort(b)) << 16);
 }
 
-// Writes 32 consecutive values v[0..31] (scaled already) as elements of T.
-template <typename T>
-__device__ __forceinline__ void store_row32(T* dst, const float (&v)[32]) {
-  if constexpr (sizeof(T) == 2) {
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 u;
-      u.x = pack2(to_elem<T>(v[8 * q + 0]), to_elem<T>(v[8 * q + 1]));
-      u.y = pack2(to_elem<T>(v[8 * q + 2]), to_elem<T>(v[8 * q + 3]));
-      u.z = pack2(to_elem<T>(v[8 * q + 4]), to_elem<T>(v[8 * q + 5]));
-      u.w = pack2(to_elem<T>(v[8 * q + 6]), to_elem<T>(v[8 * q + 7]));
-      d4[q] = u;
-    }
-  } else {
-    float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      d4[q] = make_float4(to_elem<T>(v[4 * q]), to_elem<T>(v[4 * q + 1]), to_elem<T>(v[4 * q + 2]),
-                          to_elem<T>(v[4 * q + 3]));
-  }
-}
-
 __device__ __forceinline__ float load_out_elem(const void* p, int64_t i, int dt) {
   if (dt == NIMBLE_DTYPE_F32) return static_cast<const float*>(p)[i];
   if (dt == NIMBLE_DTYPE_F16) return __half2float(static_cast<const __half*>(p)[i]);
@@ -172,8 +153,8 @@ __device__ __forceinline__ void store_out_elem(void* p, int64_t i, int dt, float
 // and its epilogue warps write them. Loads are never multicast.
 template <typename T, int EPI, bool kAMN, bool kBMN, int kCG>
 __global__ void __launch_bounds__(kThreads, 1)
-tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
-                  int N, int K, int group_m, EpiParams ep) {
+tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int group_m, EpiParams ep) {
   constexpr int kS = kCG == 2 ? kStagesPair : kStages;   // ring depth
   constexpr int kBRows = kBN / kCG;                       // B rows loaded per CTA
   constexpr int kBBytesCta = kBRows * kBKBytes;
@@ -182,7 +163,8 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kS * kABytes;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + kS * kBBytesCta);
+  uint8_t* sStore = sB + kS * kBBytesCta;  // 1024-aligned: stage sizes are multiples of 1 KiB
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sStore + kStoreBytes);
   uint64_t* empty_bar = full_bar + kS;
   uint64_t* tfull_bar = empty_bar + kS;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -353,6 +335,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       }
     };
     int it = 0;
+    int store_seq = 0;  // G staging stores issued by this warp
     for (int t = unit0; t < tiles; t += units, ++it) {
       int mb, nb;
       tile_coords(t, m_tiles, n_tiles, group_m, mb, nb);
@@ -421,7 +404,15 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         const int tcol = (rel >= 0 && rel < ncols) ? static_cast<int>(rel) : -1;
         const float lse_l2 = live ? ep.lse[row] * kLog2e : 0.0f;
         const float gs = live ? ep.gscale : 0.0f;
-        T* g = static_cast<T*>(ep.g);
+        // The warp's 32 rows x 32 columns of G go through a swizzled staging
+        // buffer and one TMA store (rows >= M / columns >= N are clipped by
+        // the tensor map). Row bytes: 64 (16-bit, 64-byte swizzle) or 128
+        // (fp32, 128-byte swizzle).
+        constexpr int kRowBytes = 32 * kElem;
+        constexpr int kChunks = kRowBytes / 16;
+        const int swz = kElem == 2 ? ((lane >> 1) & 3) : (lane & 7);
+        uint8_t* wbuf = sStore + (warp - 2) * 2 * kStoreBuf;
+        const int store_row0 = mb * kTileM + static_cast<int>(rank) * kBM + wq * 32;
 #pragma unroll 1
         for (int c = 0; c < kBN / 32; ++c) {
           if (c * 32 >= ncols) break;
@@ -437,8 +428,23 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             if (j == jt) p -= 1.0f;
             v[j] = p * gs;
           }
-          const int64_t col = col0_tile + c * 32;
-          if (row_ok) store_row32<T>(g + row * ep.ldg + col, v);
+          uint8_t* buf = wbuf + (store_seq & 1) * kStoreBuf;
+          if (store_seq >= 2 && lane == 0) ptx::bulk_wait_read<1>();  // buffer's previous store has read it
+          __syncwarp();
+          alignas(16) T vals[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) vals[j] = to_elem<T>(v[j]);
+#pragma unroll
+          for (int q = 0; q < kChunks; ++q)
+            *reinterpret_cast<uint4*>(buf + lane * kRowBytes + ((q ^ swz) * 16)) =
+                *reinterpret_cast<const uint4*>(&vals[q * (16 / kElem)]);
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_2d(&tmC, buf, static_cast<int>(col0_tile) + c * 32, store_row0);
+            ptx::bulk_commit();
+          }
+          ++store_seq;
         }
         release(acc);
       } else {  // EPI_STORE
@@ -525,6 +531,11 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         }
         release(acc);
       }
+    }
+    // Every G store must have landed before the CTA exits.
+    if constexpr (EPI == EPI_CE_GRAD) {
+      if (lane == 0) ptx::bulk_wait<0>();
+      __syncwarp();
     }
   }
 
@@ -719,6 +730,26 @@ const int g_group_m = [] {
   return g > 0 ? g : 16;
 }();
 
+// Row-major [rows x cols] output written by 32 x 32 TMA box stores from a
+// swizzled staging buffer (64-byte swizzle for 16-bit rows of 64 B, 128-byte
+// swizzle for fp32 rows of 128 B).
+int make_store_map(CUtensorMap* map, const void* base, int dtype, int64_t cols, int64_t rows, int64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return fail(NIMBLE_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled entry point unavailable");
+  const int es = elem_size(dtype);
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * es) % 16 != 0)
+    return fail(NIMBLE_ERR_INVALID_ARG, "store target is not 16-byte aligned");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * es)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, tmap_dtype(dtype), 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, es == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NIMBLE_ERR_CUDA, "cuTensorMapEncodeTiled (store) failed: " + std::to_string(r));
+  return NIMBLE_OK;
+}
+
 struct DevInfo {
   int sms = 0;
   int major = 0;
@@ -751,8 +782,13 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t 
     return fail(NIMBLE_ERR_INVALID_ARG, "GEMM extent exceeds 2^31");
   DevInfo di;
   if (int rc = device_info(&di)) return rc;
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mc;
   if (int rc = make_operand_map(&ma, A, dtype, kAMN, K, M, lda, kBM)) return rc;
+  if constexpr (EPI == EPI_CE_GRAD) {
+    if (int rc = make_store_map(&mc, ep.g, dtype, N, M, ep.ldg)) return rc;
+  } else {
+    mc = ma;  // unused by the other epilogues
+  }
   const bool pairs = (g_cta_pairs & gemm_kind_bit<EPI, kAMN>()) != 0;
   if (int rc = make_operand_map(&mb, B, dtype, kBMN, K, N, ldb, pairs ? kBN / 2 : kBN)) return rc;
   const int group_m = g_group_m;
@@ -775,7 +811,7 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    NIMBLE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, static_cast<int>(M), static_cast<int>(N),
+    NIMBLE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, static_cast<int>(M), static_cast<int>(N),
                                        static_cast<int>(K), group_m, ep));
   } else {
     auto kern = tc_gemm_tn_kernel<T, EPI, kAMN, kBMN, 1>;
@@ -783,7 +819,7 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t 
     const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     if (tiles > INT32_MAX) return fail(NIMBLE_ERR_INVALID_ARG, "too many tiles");
     const int grid = static_cast<int>(std::min<int64_t>(tiles, di.sms));
-    kern<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, static_cast<int>(M), static_cast<int>(N),
+    kern<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, static_cast<int>(M), static_cast<int>(N),
                                                   static_cast<int>(K), group_m, ep);
   }
   NIMBLE_CUDA_TRY(cudaGetLastError());
