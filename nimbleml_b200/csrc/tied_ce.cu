@@ -58,6 +58,8 @@ constexpr int kSmemBytes = kStages * (kABytes + kBBytes) + kStoreBytes + 1024 /*
 // CTA-pair mode (cta_group::2): each CTA holds 128 rows of A and 128 of the
 // 256 B rows per stage (32 KiB), so the ring is 6 stages deep.
 constexpr int kStagesPair = 6;
+// Wide single-CTA tiles: 32 KiB of A + 32 KiB of B per stage.
+constexpr int kStagesWide = 3;
 constexpr int kSmemBytesPair = kStagesPair * (kABytes + kBBytes / 2) + kStoreBytes + 1024 + 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -151,18 +153,26 @@ __device__ __forceinline__ void store_out_elem(void* p, int64_t i, int dt, float
 // with tcgen05.mma.cta_group::2 issued by the even CTA; each CTA loads its own
 // 128 A rows and 128 of the B rows, its TMEM holds its 128 accumulator rows,
 // and its epilogue warps write them. Loads are never multicast.
-template <typename T, int EPI, bool kAMN, bool kBMN, int kCG>
+//
+// kWide (one CTA) computes a 256 x 256 tile as two M=128 MMAs per K step that
+// share the B tile, accumulating into all 512 TMEM columns: a third fewer
+// operand bytes per FLOP than 128 x 256 tiles, but the epilogue of a tile no
+// longer overlaps the next tile's MMAs.
+template <typename T, int EPI, bool kAMN, bool kBMN, int kCG, bool kWide = false>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int group_m, EpiParams ep) {
-  constexpr int kS = kCG == 2 ? kStagesPair : kStages;   // ring depth
+  static_assert(!(kWide && kCG == 2), "wide tiles are single-CTA");
+  constexpr int kMB = kWide ? 2 : 1;                      // 128-row M blocks per CTA
+  constexpr int kS = kCG == 2 ? kStagesPair : (kWide ? kStagesWide : kStages);  // ring depth
   constexpr int kBRows = kBN / kCG;                       // B rows loaded per CTA
   constexpr int kBBytesCta = kBRows * kBKBytes;
-  constexpr int kTileM = kBM * kCG;                       // accumulator rows per tile
+  constexpr int kABytesCta = kABytes * kMB;
+  constexpr int kTileM = kBM * kCG * kMB;                 // accumulator rows per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + kS * kABytes;
+  uint8_t* sB = smem + kS * kABytesCta;
   uint8_t* sStore = sB + kS * kBBytesCta;  // 1024-aligned: stage sizes are multiples of 1 KiB
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sStore + kStoreBytes);
   uint64_t* empty_bar = full_bar + kS;
@@ -233,13 +243,15 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!ptx::mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) { ok = false; break; }
           // The even CTA's full barrier counts both CTAs' bytes.
-          if (leader) ptx::mbar_arrive_expect_tx(&full_bar[stage], kCG * (kABytes + kBBytesCta));
+          if (leader) ptx::mbar_arrive_expect_tx(&full_bar[stage], kCG * (kABytesCta + kBBytesCta));
           if constexpr (kAMN) {
 #pragma unroll
-            for (int j = 0; j < kBM / kBK; ++j)
-              load(sA + stage * kABytes + j * kBK * 128, &tmA, stage, a_row0 + j * kBK, kb * kBK);
+            for (int j = 0; j < kMB * kBM / kBK; ++j)
+              load(sA + stage * kABytesCta + j * kBK * 128, &tmA, stage, a_row0 + j * kBK, kb * kBK);
           } else {
-            load(sA + stage * kABytes, &tmA, stage, kb * kBK, a_row0);
+#pragma unroll
+            for (int q = 0; q < kMB; ++q)
+              load(sA + stage * kABytesCta + q * kABytes, &tmA, stage, kb * kBK, a_row0 + q * kBM);
           }
           if constexpr (kBMN) {
 #pragma unroll
@@ -268,7 +280,8 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = ptx::idesc_f32acc(ElemInfo<T>::kFmt, kTileM, kBN, kAMN, kBMN);
+      // M of one instruction: 128 per CTA, 256 for a CTA pair (never the wide tile's 256).
+      constexpr uint32_t idesc = ptx::idesc_f32acc(ElemInfo<T>::kFmt, kBM * kCG, kBN, kAMN, kBMN);
       // Start-address step (16-byte units) per MMA along K: 32 bytes inside a
       // K-major swizzle row, or kUK rows of 128 bytes for an MN-major tile.
       constexpr uint64_t kAStep = kAMN ? kUK * 128 / 16 : 2;
@@ -278,15 +291,15 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       int it = 0;
       bool ok = true;
       for (int t = unit0; t < tiles && ok; t += units, ++it) {
-        const int acc = it & 1;
-        const uint32_t aphase = (it >> 1) & 1;
+        const int acc = kWide ? 0 : (it & 1);
+        const uint32_t aphase = kWide ? (it & 1) : ((it >> 1) & 1);
         if (!ptx::mbar_wait(&tempty_bar[acc], aphase ^ 1, abort_flag)) { ok = false; break; }
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!ptx::mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
-          const uint32_t a_addr = ptx::smem_u32(sA + stage * kABytes);
+          const uint32_t a_addr = ptx::smem_u32(sA + stage * kABytesCta);
           const uint32_t b_addr = ptx::smem_u32(sB + stage * kBBytesCta);
           const uint64_t adesc = kAMN ? ptx::sdesc_mn_sw128(a_addr, kBK * 128, kTF32) : ptx::sdesc_k_sw128(a_addr);
           const uint64_t bdesc = kBMN ? ptx::sdesc_mn_sw128(b_addr, kBK * 128, kTF32) : ptx::sdesc_k_sw128(b_addr);
@@ -296,6 +309,11 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
               ptx::umma_pair<kTF32>(d_tmem, adesc + kAStep * k, bdesc + kBStep * k, idesc, (kb | k) != 0 ? 1u : 0u);
             else
               ptx::umma<kTF32>(d_tmem, adesc + kAStep * k, bdesc + kBStep * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (kWide) {
+              // Second M block: A rows 128..255 sit 16 KiB further in the stage.
+              ptx::umma<kTF32>(d_tmem + kBN, adesc + (kABytes >> 4) + kAStep * k, bdesc + kBStep * k, idesc,
+                               (kb | k) != 0 ? 1u : 0u);
+            }
           }
           // Frees this stage in both CTAs once the MMAs have read it.
           if constexpr (kCG == 2) ptx::umma_commit_pair(&empty_bar[stage], 0x3);
@@ -339,14 +357,17 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     for (int t = unit0; t < tiles; t += units, ++it) {
       int mb, nb;
       tile_coords(t, m_tiles, n_tiles, group_m, mb, nb);
-      const int acc = it & 1;
-      const uint32_t aphase = (it >> 1) & 1;
+      const int acc = kWide ? 0 : (it & 1);
+      const uint32_t aphase = kWide ? (it & 1) : ((it >> 1) & 1);
       bool ok = ptx::mbar_wait(&tfull_bar[acc], aphase, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       ptx::tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kBN;
-      const int64_t row = static_cast<int64_t>(mb) * kTileM + static_cast<int64_t>(rank) * kBM + row_t;
+#pragma unroll 1
+      for (int rb = 0; rb < kMB; ++rb) {
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + (acc + rb) * kBN;
+      const int64_t row =
+          static_cast<int64_t>(mb) * kTileM + static_cast<int64_t>(rank) * kBM + rb * kBM + row_t;
       const bool row_ok = row < M;
       const int ncols = min(kBN, N - nb * kBN);
       const int64_t col0_tile = static_cast<int64_t>(nb) * kBN;
@@ -392,7 +413,6 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
               if (j == jt) tval = v[j];
           }
         }
-        release(acc);
         if (row_ok) {
           ep.part[static_cast<int64_t>(nb) * M + row] = make_float2(mrun, srun);
           if (tcol >= 0) ep.tgt[row] = tval;
@@ -412,7 +432,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         constexpr int kChunks = kRowBytes / 16;
         const int swz = kElem == 2 ? ((lane >> 1) & 3) : (lane & 7);
         uint8_t* wbuf = sStore + (warp - 2) * 2 * kStoreBuf;
-        const int store_row0 = mb * kTileM + static_cast<int>(rank) * kBM + wq * 32;
+        const int store_row0 = mb * kTileM + static_cast<int>(rank) * kBM + rb * kBM + wq * 32;
 #pragma unroll 1
         for (int c = 0; c < kBN / 32; ++c) {
           if (c * 32 >= ncols) break;
@@ -446,7 +466,6 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           }
           ++store_seq;
         }
-        release(acc);
       } else {  // EPI_STORE
 #pragma unroll 1
         for (int c = 0; c < kBN / 32; ++c) {
@@ -529,8 +548,9 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             }
           }
         }
-        release(acc);
       }
+      }  // row blocks
+      release(acc);
     }
     // Every G store must have landed before the CTA exits.
     if constexpr (EPI == EPI_CE_GRAD) {
@@ -719,6 +739,17 @@ const int g_cta_pairs = [] {
   const int m = std::atoi(v);
   return m == 1 ? 15 : m;
 }();
+// Wide single-CTA 256 x 256 tiles, same bit mask (NIMBLEML_TIED_CE_WIDE).
+// Default 14: the three backward GEMMs use wide tiles (a third fewer operand
+// bytes per FLOP lets them run at higher clocks under the power cap), the
+// forward keeps 128 x 256 tiles whose epilogue overlaps the next tile's MMAs.
+const int g_wide = [] {
+  const char* v = std::getenv("NIMBLEML_TIED_CE_WIDE");
+  if (!v) return 14;
+  const int m = std::atoi(v);
+  return m == 1 ? 15 : m;
+}();
+constexpr int kSmemBytesWide = kStagesWide * (2 * kABytes + kBBytes) + kStoreBytes + 1024 + 256;
 template <int EPI, bool kAMN>
 constexpr int gemm_kind_bit() {
   return EPI == EPI_CE_FWD ? 1 : EPI == EPI_CE_GRAD ? 2 : kAMN ? 4 : 8;
@@ -813,6 +844,14 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t 
     cfg.numAttrs = 1;
     NIMBLE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, static_cast<int>(M), static_cast<int>(N),
                                        static_cast<int>(K), group_m, ep));
+  } else if (g_wide & gemm_kind_bit<EPI, kAMN>()) {
+    auto kern = tc_gemm_tn_kernel<T, EPI, kAMN, kBMN, 1, true>;
+    NIMBLE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytesWide));
+    const int64_t tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
+    if (tiles > INT32_MAX) return fail(NIMBLE_ERR_INVALID_ARG, "too many tiles");
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, di.sms));
+    kern<<<grid, kThreads, kSmemBytesWide, stream>>>(ma, mb, mc, static_cast<int>(M), static_cast<int>(N),
+                                                      static_cast<int>(K), group_m, ep);
   } else {
     auto kern = tc_gemm_tn_kernel<T, EPI, kAMN, kBMN, 1>;
     NIMBLE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
