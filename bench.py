@@ -405,10 +405,10 @@ def main():
         stats3 = vp.gather_shard_stats(part, group)
         _, _, lse, loss, valid = k.combine(stats3, labels, v, ign)
         st = k.TiedCEStats(lse=lse, valid_count=valid, ignore_index=ign, vocab_size=v, vocab_offset=v_off)
-        dh, de = k.shard_backward(ones, h, e_local, labels, st,
-                                  grad_hidden_dtype=torch.float32 if world > 1 else None)
         if world > 1:
-            vp.reduce_grad_hidden(dh, group)
+            vp.sharded_backward(ones, h, e_local, labels, st, group)
+        else:
+            k.shard_backward(ones, h, e_local, labels, st)
         return loss
 
     def barrier():
@@ -459,7 +459,11 @@ def main():
         lossfn = CrossEntropyLoss()
 
         def e2e_step():
-            hd = h_host.to(dev, non_blocking=True).requires_grad_(True)
+            if head is None:
+                hd = h_host.to(dev, non_blocking=True).requires_grad_(True)
+            else:
+                # Replicated h: each rank copies its 1/P rows, NVLink all_gather does the rest.
+                hd = head.hidden_from_host(h_host).requires_grad_(True)
             yd = y_host.to(dev, non_blocking=True)
             w_param.grad = None
             if head is None:
@@ -482,8 +486,8 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             te = float(t[0])
         e2e = {"value": n * args.steps / te, "unit": "tokens/s",
-               "h2d_bytes_per_step": h_host.numel() * h_host.element_size() + y_host.numel() * 8,
-               "d2h_bytes_per_step": 4 if world == 1 else 4}
+               "h2d_bytes_per_step": h_host.numel() * h_host.element_size() // world + y_host.numel() * 8,
+               "d2h_bytes_per_step": 4, "bytes_are": "per rank"}
 
     if rank != 0:
         dist.barrier() if world > 1 else None

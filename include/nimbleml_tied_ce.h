@@ -66,6 +66,26 @@ enum {
   NIMBLE_STATUS_WAIT_TIMEOUT = 2   /* a bounded device wait gave up (kernel aborted)  */
 };
 
+/* nimble_tied_ce_backward for vocab-sharded ranks that overlap the grad_hidden
+ * reduction with compute (no counterpart in the reference, which has no
+ * multi-GPU path). Same arguments and results, plus: the last slab computes
+ * grad_hidden before its grad_weights rows and records
+ * grad_hidden_ready_event (a cudaEvent_t) on `stream` right after it; the
+ * last grad_weights GEMM then runs on at most last_de_max_ctas SMs (0 = all),
+ * leaving SMs for a collective the caller enqueues on another stream after
+ * waiting on the event. */
+NIMBLE_API int nimble_tied_ce_backward_overlap(const float* grad_scale, const void* hidden,
+                                               const void* weights, const int64_t* labels,
+                                               const float* lse, const float* valid_count,
+                                               int64_t n_tokens, int64_t d_model, int64_t v_local,
+                                               int64_t v_offset, int64_t ignore_index, int dtype,
+                                               void* grad_hidden, int grad_hidden_dtype,
+                                               void* grad_weights, int grad_weights_dtype,
+                                               int accumulate_grad_weights, size_t slab_bytes,
+                                               void* workspace, size_t workspace_bytes, int* status,
+                                               void* stream, void* grad_hidden_ready_event,
+                                               int last_de_max_ctas);
+
 /* 1 when a compute-capability 10.x device is visible, else 0. Mirrors the
  * reference's availability flags (native/src/module.cpp:13-17,221-227). */
 NIMBLE_API int nimble_tied_ce_available(void);

@@ -93,6 +93,11 @@ SIGNATURES = {
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
          _c_int, _c_vp, _c_int, _c_vp, _c_int, _c_int, _c_size, _c_vp, _c_size, _c_vp,
          _c_vp]),
+    "nimble_tied_ce_backward_overlap": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+         _c_int, _c_vp, _c_int, _c_vp, _c_int, _c_int, _c_size, _c_vp, _c_size, _c_vp,
+         _c_vp, _c_vp, _c_int]),
 }
 
 

@@ -807,12 +807,14 @@ int device_info(DevInfo* info) {
 // row-major [M x K] (K-major) or [K x M] (kAMN); likewise B.
 template <typename T, int EPI, bool kAMN, bool kBMN>
 int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N, int64_t K, int dtype,
-                const EpiParams& ep, cudaStream_t stream) {
+                const EpiParams& ep, cudaStream_t stream, int max_ctas) {
   if (M <= 0 || N <= 0 || K <= 0) return NIMBLE_OK;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
     return fail(NIMBLE_ERR_INVALID_ARG, "GEMM extent exceeds 2^31");
   DevInfo di;
   if (int rc = device_info(&di)) return rc;
+  // A cap leaves SMs free for work that should overlap this GEMM (NCCL).
+  if (max_ctas > 0 && max_ctas < di.sms) di.sms = max_ctas;
   CUtensorMap ma, mb, mc;
   if (int rc = make_operand_map(&ma, A, dtype, kAMN, K, M, lda, kBM)) return rc;
   if constexpr (EPI == EPI_CE_GRAD) {
@@ -867,14 +869,14 @@ int launch_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int64_t 
 
 template <int EPI, bool kAMN = false, bool kBMN = false>
 int gemm_dispatch(int dtype, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
-                  int64_t K, const EpiParams& ep, cudaStream_t s) {
+                  int64_t K, const EpiParams& ep, cudaStream_t s, int max_ctas = 0) {
   switch (dtype) {
     case NIMBLE_DTYPE_F16:
-      return launch_gemm<__half, EPI, kAMN, kBMN>(A, lda, B, ldb, M, N, K, dtype, ep, s);
+      return launch_gemm<__half, EPI, kAMN, kBMN>(A, lda, B, ldb, M, N, K, dtype, ep, s, max_ctas);
     case NIMBLE_DTYPE_BF16:
-      return launch_gemm<__nv_bfloat16, EPI, kAMN, kBMN>(A, lda, B, ldb, M, N, K, dtype, ep, s);
+      return launch_gemm<__nv_bfloat16, EPI, kAMN, kBMN>(A, lda, B, ldb, M, N, K, dtype, ep, s, max_ctas);
     case NIMBLE_DTYPE_F32:
-      return launch_gemm<float, EPI, kAMN, kBMN>(A, lda, B, ldb, M, N, K, dtype, ep, s);
+      return launch_gemm<float, EPI, kAMN, kBMN>(A, lda, B, ldb, M, N, K, dtype, ep, s, max_ctas);
   }
   return fail(NIMBLE_ERR_INVALID_ARG, "unknown dtype");
 }
@@ -1039,13 +1041,13 @@ extern "C" int nimble_tied_ce_backward_workspace_size(int64_t n_tokens, int64_t 
   return NIMBLE_OK;
 }
 
-extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidden, const void* weights,
-                                       const int64_t* labels, const float* lse, const float* valid_count,
-                                       int64_t n_tokens, int64_t d_model, int64_t v_local, int64_t v_offset,
-                                       int64_t ignore_index, int dtype, void* grad_hidden, int grad_hidden_dtype,
-                                       void* grad_weights, int grad_weights_dtype, int accumulate_grad_weights,
-                                       size_t slab_bytes, void* workspace, size_t workspace_bytes, int* status,
-                                       void* stream) {
+namespace {
+int backward_impl(const float* grad_scale, const void* hidden, const void* weights, const int64_t* labels,
+                  const float* lse, const float* valid_count, int64_t n_tokens, int64_t d_model, int64_t v_local,
+                  int64_t v_offset, int64_t ignore_index, int dtype, void* grad_hidden, int grad_hidden_dtype,
+                  void* grad_weights, int grad_weights_dtype, int accumulate_grad_weights, size_t slab_bytes,
+                  void* workspace, size_t workspace_bytes, int* status, void* stream, void* dh_done_event,
+                  int last_de_max_ctas) {
   if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype)) return rc;
   if (!grad_hidden || !grad_weights || !grad_scale || !lse || !valid_count)
     return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
@@ -1097,42 +1099,85 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
     eg.gscale = gscale;
     eg.status = status;
     if (int rc = gemm_dispatch<EPI_CE_GRAD>(dtype, h, d_model, E_sl, d_model, n_tokens, vc, d_model, eg, s)) return rc;
+    const bool last = sl == L.n_slabs - 1;
     // 2) dE[c0:c0+vc] = G^T h: A = G read MN-major ([tokens x vc]), B = h
     //    read MN-major ([tokens x d]); K = tokens.
-    EpiParams ee{};
-    ee.out = static_cast<uint8_t*>(grad_weights) + elem_size(grad_weights_dtype) * c0 * d_model;
-    ee.ld_out = d_model;
-    ee.out_dtype = grad_weights_dtype;
-    ee.alpha_num = grad_scale;
-    ee.alpha_den = valid_count;
-    ee.alpha_mult = 1.0f / gscale;
-    ee.accum_out = accumulate_grad_weights ? 1 : 0;
-    ee.status = status;
-    if (int rc = gemm_dispatch<EPI_STORE, true, true>(dtype, g, L.slab, h, d_model, vc, d_model, n_tokens, ee, s))
-      return rc;
+    auto run_de = [&](int max_ctas) -> int {
+      EpiParams ee{};
+      ee.out = static_cast<uint8_t*>(grad_weights) + elem_size(grad_weights_dtype) * c0 * d_model;
+      ee.ld_out = d_model;
+      ee.out_dtype = grad_weights_dtype;
+      ee.alpha_num = grad_scale;
+      ee.alpha_den = valid_count;
+      ee.alpha_mult = 1.0f / gscale;
+      ee.accum_out = accumulate_grad_weights ? 1 : 0;
+      ee.status = status;
+      return gemm_dispatch<EPI_STORE, true, true>(dtype, g, L.slab, h, d_model, vc, d_model, n_tokens, ee, s,
+                                                  max_ctas);
+    };
     // 3) dh (+)= G E[c0:c0+vc]: A = G K-major, B = E slab read MN-major
     //    ([vc x d]); K = slab columns.
-    EpiParams eh{};
-    eh.status = status;
-    const bool last = sl == L.n_slabs - 1;
-    if (last) {
-      eh.out = grad_hidden;
-      eh.out_dtype = grad_hidden_dtype;
-      eh.alpha_num = grad_scale;
-      eh.alpha_den = valid_count;
-      eh.alpha_mult = 1.0f / gscale;
+    auto run_dh = [&]() -> int {
+      EpiParams eh{};
+      eh.status = status;
+      if (last) {
+        eh.out = grad_hidden;
+        eh.out_dtype = grad_hidden_dtype;
+        eh.alpha_num = grad_scale;
+        eh.alpha_den = valid_count;
+        eh.alpha_mult = 1.0f / gscale;
+      } else {
+        eh.out = dh_acc;
+        eh.out_dtype = NIMBLE_DTYPE_F32;
+        eh.alpha_mult = 1.0f;
+      }
+      eh.ld_out = d_model;
+      eh.src = sl > 0 ? dh_acc : nullptr;
+      eh.ld_src = d_model;
+      return gemm_dispatch<EPI_STORE, false, true>(dtype, g, L.slab, E_sl, d_model, n_tokens, d_model, vc, eh, s);
+    };
+    if (last && dh_done_event) {
+      // grad_hidden is final after this slab's dh GEMM: announce it, then
+      // run the last dE GEMM (optionally on fewer SMs) while the caller
+      // reduces grad_hidden across ranks.
+      if (int rc = run_dh()) return rc;
+      NIMBLE_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(dh_done_event), s));
+      if (int rc = run_de(last_de_max_ctas)) return rc;
     } else {
-      eh.out = dh_acc;
-      eh.out_dtype = NIMBLE_DTYPE_F32;
-      eh.alpha_mult = 1.0f;
+      if (int rc = run_de(0)) return rc;
+      if (int rc = run_dh()) return rc;
     }
-    eh.ld_out = d_model;
-    eh.src = sl > 0 ? dh_acc : nullptr;
-    eh.ld_src = d_model;
-    if (int rc = gemm_dispatch<EPI_STORE, false, true>(dtype, g, L.slab, E_sl, d_model, n_tokens, d_model, vc, eh, s))
-      return rc;
   }
   return NIMBLE_OK;
+}
+}  // namespace
+
+extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidden, const void* weights,
+                                       const int64_t* labels, const float* lse, const float* valid_count,
+                                       int64_t n_tokens, int64_t d_model, int64_t v_local, int64_t v_offset,
+                                       int64_t ignore_index, int dtype, void* grad_hidden, int grad_hidden_dtype,
+                                       void* grad_weights, int grad_weights_dtype, int accumulate_grad_weights,
+                                       size_t slab_bytes, void* workspace, size_t workspace_bytes, int* status,
+                                       void* stream) {
+  return backward_impl(grad_scale, hidden, weights, labels, lse, valid_count, n_tokens, d_model, v_local, v_offset,
+                       ignore_index, dtype, grad_hidden, grad_hidden_dtype, grad_weights, grad_weights_dtype,
+                       accumulate_grad_weights, slab_bytes, workspace, workspace_bytes, status, stream, nullptr, 0);
+}
+
+extern "C" int nimble_tied_ce_backward_overlap(const float* grad_scale, const void* hidden, const void* weights,
+                                               const int64_t* labels, const float* lse, const float* valid_count,
+                                               int64_t n_tokens, int64_t d_model, int64_t v_local, int64_t v_offset,
+                                               int64_t ignore_index, int dtype, void* grad_hidden,
+                                               int grad_hidden_dtype, void* grad_weights, int grad_weights_dtype,
+                                               int accumulate_grad_weights, size_t slab_bytes, void* workspace,
+                                               size_t workspace_bytes, int* status, void* stream,
+                                               void* grad_hidden_ready_event, int last_de_max_ctas) {
+  if (!grad_hidden_ready_event) return fail(NIMBLE_ERR_INVALID_ARG, "null grad_hidden_ready_event");
+  if (last_de_max_ctas < 0) return fail(NIMBLE_ERR_INVALID_ARG, "last_de_max_ctas must be >= 0");
+  return backward_impl(grad_scale, hidden, weights, labels, lse, valid_count, n_tokens, d_model, v_local, v_offset,
+                       ignore_index, dtype, grad_hidden, grad_hidden_dtype, grad_weights, grad_weights_dtype,
+                       accumulate_grad_weights, slab_bytes, workspace, workspace_bytes, status, stream,
+                       grad_hidden_ready_event, last_de_max_ctas);
 }
 
 // ================================================================ diagnostics

@@ -161,11 +161,15 @@ def combine(shard_stats: torch.Tensor, labels: torch.Tensor, vocab_size: int, ig
 
 def shard_backward(grad_scale: torch.Tensor, h: torch.Tensor, w: torch.Tensor, labels: torch.Tensor,
                    stats: TiedCEStats, *, grad_hidden_dtype=None, grad_weights: Optional[torch.Tensor] = None,
-                   accumulate: bool = False, slab_bytes: Optional[int] = None):
+                   accumulate: bool = False, slab_bytes: Optional[int] = None,
+                   ready_event: Optional[torch.cuda.Event] = None, last_de_max_ctas: int = 0):
     """(grad_hidden partial over this shard, grad_weights of the shard).
 
     ``slab_bytes`` bounds the vocab slab's G scratch (default: the
     NIMBLEML_TIED_CE_SLAB_BYTES environment value, else the library's 2 GiB).
+    With ``ready_event`` the event is recorded as soon as grad_hidden is final
+    and the last grad_weights GEMM runs on at most ``last_de_max_ctas`` SMs,
+    so a collective on grad_hidden can overlap it.
     """
     n, d = h.shape
     v_local = w.shape[0]
@@ -179,12 +183,15 @@ def shard_backward(grad_scale: torch.Tensor, h: torch.Tensor, w: torch.Tensor, l
     slab = SLAB_BYTES if slab_bytes is None else int(slab_bytes)
     ws = _workspace(native.backward_workspace_size(n, d, v_local, dt, slab), dev)
     gs = grad_scale.reshape(-1)[:1].to(device=dev, dtype=torch.float32).contiguous()
-    native.call(
-        "nimble_tied_ce_backward", gs.data_ptr(), h.data_ptr(), w.data_ptr(), labels.data_ptr(),
-        stats.lse.data_ptr(), stats.valid_count.data_ptr(), n, d, v_local, stats.vocab_offset,
-        stats.ignore_index, dt, grad_h.data_ptr(), _TORCH_TO_NIMBLE[gh_dtype], grad_weights.data_ptr(),
-        _TORCH_TO_NIMBLE[grad_weights.dtype], 1 if accumulate else 0, slab, ws.data_ptr(),
-        ws.numel(), status_word(dev).data_ptr(), _stream_ptr(dev))
+    args = (gs.data_ptr(), h.data_ptr(), w.data_ptr(), labels.data_ptr(), stats.lse.data_ptr(),
+            stats.valid_count.data_ptr(), n, d, v_local, stats.vocab_offset, stats.ignore_index, dt,
+            grad_h.data_ptr(), _TORCH_TO_NIMBLE[gh_dtype], grad_weights.data_ptr(),
+            _TORCH_TO_NIMBLE[grad_weights.dtype], 1 if accumulate else 0, slab, ws.data_ptr(), ws.numel(),
+            status_word(dev).data_ptr(), _stream_ptr(dev))
+    if ready_event is None:
+        native.call("nimble_tied_ce_backward", *args)
+    else:
+        native.call("nimble_tied_ce_backward_overlap", *args, ready_event.cuda_event, int(last_de_max_ctas))
     return grad_h, grad_weights
 
 

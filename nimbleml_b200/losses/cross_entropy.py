@@ -72,11 +72,12 @@ class _TiedCrossEntropy(torch.autograd.Function):
                             vocab_size=vocab_size, vocab_offset=vocab_offset)
         sharded = vocab_parallel.world_size(group) > 1
         grad_w = torch.empty(weights.shape, dtype=w_dtype, device=weights.device)
-        grad_h, grad_w = shard_backward(
-            grad_out, h2d, weights, labels, stats,
-            grad_hidden_dtype=torch.float32 if sharded else None, grad_weights=grad_w)
         if sharded:
-            grad_h = vocab_parallel.reduce_grad_hidden(grad_h, group).to(h2d.dtype)
+            grad_h, grad_w = vocab_parallel.sharded_backward(grad_out, h2d, weights, labels, stats, group,
+                                                             grad_weights=grad_w)
+            grad_h = grad_h.to(h2d.dtype)
+        else:
+            grad_h, grad_w = shard_backward(grad_out, h2d, weights, labels, stats, grad_weights=grad_w)
         if CHECK_BOUNDS:
             check_status(h2d.device)
         return grad_h, grad_w, None, None, None, None, None

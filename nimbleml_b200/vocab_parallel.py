@@ -19,8 +19,15 @@ from __future__ import annotations
 
 from typing import Optional, Tuple
 
+import os
+
 import torch
 import torch.distributed as dist
+
+# SMs left free for the grad_hidden all_reduce while the last grad_weights
+# GEMM runs (NIMBLEML_TIED_CE_COMM_SMS, default 16).
+COMM_SMS = int(os.environ.get("NIMBLEML_TIED_CE_COMM_SMS", "16"))
+_comm_streams: dict = {}
 
 
 def world_size(group=None) -> int:
@@ -63,6 +70,43 @@ def reduce_grad_hidden(grad_h: torch.Tensor, group=None) -> torch.Tensor:
     return grad_h
 
 
+def _comm_stream(device: torch.device) -> torch.cuda.Stream:
+    key = device.index
+    st = _comm_streams.get(key)
+    if st is None:
+        st = torch.cuda.Stream(device=device)
+        _comm_streams[key] = st
+    return st
+
+
+def sharded_backward(grad_scale, h, w, labels, stats, group=None, *, grad_weights=None, accumulate=False):
+    """Backward of one vocab shard with the grad_hidden all_reduce overlapped.
+
+    The library computes the last slab's grad_hidden first and records an
+    event; the fp32 all_reduce then runs on a side stream while the last
+    grad_weights GEMM runs on all but COMM_SMS SMs. Returns (grad_hidden
+    summed over ranks, fp32; grad_weights of this shard).
+    """
+    from nimbleml_b200.kernels.fused_tied_crossentropy import shard_backward
+
+    if world_size(group) == 1:
+        return shard_backward(grad_scale, h, w, labels, stats, grad_weights=grad_weights, accumulate=accumulate)
+    dev = h.device
+    ready = torch.cuda.Event()
+    ready.record()  # creates the event; re-recorded by the library
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    grad_h, grad_w = shard_backward(grad_scale, h, w, labels, stats, grad_hidden_dtype=torch.float32,
+                                    grad_weights=grad_weights, accumulate=accumulate, ready_event=ready,
+                                    last_de_max_ctas=max(1, sms - COMM_SMS))
+    comm = _comm_stream(dev)
+    comm.wait_event(ready)
+    with torch.cuda.stream(comm):
+        dist.all_reduce(grad_h, op=dist.ReduceOp.SUM, group=group)
+    grad_h.record_stream(comm)
+    torch.cuda.current_stream(dev).wait_stream(comm)
+    return grad_h, grad_w
+
+
 class VocabParallelTiedHead:
     """Holds this rank's shard of the tied matrix and applies the sharded loss."""
 
@@ -80,6 +124,26 @@ class VocabParallelTiedHead:
         if shard.shape[0] != self.rows:
             raise ValueError(f"shard has {shard.shape[0]} rows, expected {self.rows}")
         self.weights = shard.contiguous()
+
+    def hidden_from_host(self, hidden_host: torch.Tensor) -> torch.Tensor:
+        """Replicates host-resident hidden states (N, d) on every rank's GPU.
+
+        Each rank copies only its 1/P slice of the rows from host memory
+        (pinned for an asynchronous copy) and one all_gather over NVLink
+        assembles the rest, so PCIe traffic per rank falls from N*d to
+        N*d/P elements. Returns a device tensor (not a leaf of any graph).
+        """
+        if self.world == 1:
+            return hidden_host.to(self.weights.device, non_blocking=True)
+        n, d = hidden_host.shape
+        per = -(-n // self.world)
+        lo, hi = min(self.rank * per, n), min((self.rank + 1) * per, n)
+        dev = self.weights.device
+        chunk = torch.zeros((per, d), dtype=hidden_host.dtype, device=dev)
+        chunk[: hi - lo].copy_(hidden_host[lo:hi], non_blocking=True)
+        full = torch.empty((per * self.world, d), dtype=hidden_host.dtype, device=dev)
+        dist.all_gather_into_tensor(full, chunk, group=self.group)
+        return full[:n]
 
     def loss(self, hidden2d: torch.Tensor, labels: torch.Tensor, ignore_index: Optional[int] = None):
         from nimbleml_b200.losses.cross_entropy import tied_cross_entropy

@@ -285,3 +285,22 @@ def test_headline_shape_full_size_properties():
     de_ref = (pc / n).T @ hf
     assert rel(den[torch.as_tensor(cls).cuda()].cpu().numpy(), de_ref) < 1e-2
     _ = tgt
+
+
+def test_overlap_entry_point_matches_backward():
+    """nimble_tied_ce_backward_overlap (event after grad_hidden, capped last dE
+    GEMM) gives bit-identical results to nimble_tied_ce_backward."""
+    from nimbleml_b200.kernels import fused_tied_crossentropy as k
+
+    n, d, v = 640, 256, 3001
+    h, e, y = orc.make_inputs(n, d, v, seed=12, unit_rms=True)
+    hd, ed, yd = to_dev(h, torch.float16), to_dev(e, torch.float16), torch.as_tensor(y).cuda()
+    loss, hh, ww, st, mx, se = k.fused_tied_crossentropy_forward(hd, ed, yd)
+    one = torch.ones(1, device="cuda")
+    a = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32)
+    ev = torch.cuda.Event()
+    ev.record()
+    b = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32, ready_event=ev, last_de_max_ctas=20)
+    torch.cuda.synchronize()
+    assert ev.query()
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])

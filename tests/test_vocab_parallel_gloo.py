@@ -75,3 +75,34 @@ def test_gloo_two_rank_exchange_matches_single_device_math():
     # Every rank holds bit-identical results.
     assert results[0][1] == results[1][1]
     assert np.array_equal(results[0][2], results[1][2])
+
+
+def _host_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nimbleml_b200.vocab_parallel import VocabParallelTiedHead
+
+        h = torch.arange(13 * 4, dtype=torch.float32).view(13, 4)
+        head = VocabParallelTiedHead(torch.zeros(10, 4), 10, group=dist.group.WORLD)
+        q.put((rank, head.hidden_from_host(h).clone()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_hidden_from_host_assembles_all_rows():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 28500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_host_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = torch.arange(13 * 4, dtype=torch.float32).view(13, 4)
+    for _, got in res:
+        assert torch.equal(got, want)
