@@ -26,7 +26,7 @@ import torch.distributed as dist
 
 # SMs left free for the grad_hidden all_reduce while the last grad_weights
 # GEMM runs (NIMBLEML_TIED_CE_COMM_SMS, default 16).
-COMM_SMS = int(os.environ.get("NIMBLEML_TIED_CE_COMM_SMS", "16"))
+COMM_SMS = int(os.environ.get("NIMBLEML_TIED_CE_COMM_SMS", "32"))
 _comm_streams: dict = {}
 
 
