@@ -25,7 +25,8 @@ import torch
 import torch.distributed as dist
 
 # SMs left free for the grad_hidden all_reduce while the last grad_weights
-# GEMM runs (NIMBLEML_TIED_CE_COMM_SMS, default 16).
+# GEMM runs (NIMBLEML_TIED_CE_COMM_SMS, default 32; with 8 at 8 ranks NCCL is
+# starved and the reduction waits for the GEMM).
 COMM_SMS = int(os.environ.get("NIMBLEML_TIED_CE_COMM_SMS", "32"))
 _comm_streams: dict = {}
 
