@@ -942,13 +942,16 @@ BwdLayout bwd_layout(int64_t N, int64_t d, int64_t V, int dtype, size_t slab_byt
   return L;
 }
 
-int check_common(const void* h, const void* w, const int64_t* labels, int64_t N, int64_t d, int64_t V, int dtype) {
+// Shape / dtype / pointer checks shared by the entry points; `labels` may be
+// null when the entry point takes none (the tied-logits GEMMs).
+int check_common(const void* h, const void* w, const int64_t* labels, int64_t N, int64_t d, int64_t V, int dtype,
+                 bool needs_labels = true) {
   if (dtype != NIMBLE_DTYPE_F32 && dtype != NIMBLE_DTYPE_F16 && dtype != NIMBLE_DTYPE_BF16)
     return fail(NIMBLE_ERR_INVALID_ARG, "dtype must be NIMBLE_DTYPE_F32, F16 or BF16");
   if (N < 0 || d <= 0 || V <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "sizes must be positive");
   if ((d * elem_size(dtype)) % 16 != 0)
     return fail(NIMBLE_ERR_INVALID_ARG, "d_model * element size must be a multiple of 16 bytes");
-  if (N > 0 && (!h || !w || !labels)) return fail(NIMBLE_ERR_INVALID_ARG, "null input pointer");
+  if (N > 0 && (!h || !w || (needs_labels && !labels))) return fail(NIMBLE_ERR_INVALID_ARG, "null input pointer");
   return NIMBLE_OK;
 }
 
@@ -1215,8 +1218,7 @@ extern "C" int nimble_tied_logits_forward(const void* hidden, int64_t hidden_row
                                           int64_t n_rows, int64_t d_model, int64_t vocab, int dtype,
                                           void* logits, int64_t logits_row_pitch, int logits_dtype,
                                           void* stream) {
-  if (int rc = check_common(hidden, weights, reinterpret_cast<const int64_t*>(weights), n_rows, d_model, vocab,
-                            dtype))
+  if (int rc = check_common(hidden, weights, nullptr, n_rows, d_model, vocab, dtype, /*needs_labels=*/false))
     return rc;
   if (n_rows == 0) return NIMBLE_OK;
   if (!logits) return fail(NIMBLE_ERR_INVALID_ARG, "null logits pointer");
@@ -1242,8 +1244,7 @@ extern "C" int nimble_tied_logits_backward(const void* grad_logits, int64_t grad
                                            int64_t n_rows, int64_t d_model, int64_t vocab, int dtype,
                                            void* grad_hidden, int grad_hidden_dtype, void* grad_weights,
                                            int grad_weights_dtype, int accumulate_grad_weights, void* stream) {
-  if (int rc = check_common(hidden, weights, reinterpret_cast<const int64_t*>(weights), n_rows, d_model, vocab,
-                            dtype))
+  if (int rc = check_common(hidden, weights, nullptr, n_rows, d_model, vocab, dtype, /*needs_labels=*/false))
     return rc;
   if (dtype == NIMBLE_DTYPE_F32)
     return fail(NIMBLE_ERR_INVALID_ARG, "tied logits support f16 / bf16 compute");
