@@ -48,12 +48,13 @@ constexpr int kBKBytes = 128;     // one 128-byte swizzle row of K per stage
 constexpr int kStages = 4;        // shared-memory ring depth
 constexpr int kABytes = kBM * kBKBytes;  // 16 KiB
 constexpr int kBBytes = kBN * kBKBytes;  // 32 KiB
-constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kEpiWarps = 8;      // two per TMEM lane quarter, each on half the columns
+constexpr int kColHalves = kEpiWarps / 4;
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kTmemCols = 2 * kBN;  // two accumulators
-// Staging for the G tile stores: per epilogue warp two 32 x 32 buffers of up
-// to 128-byte rows (4 KiB each).
-constexpr int kStoreBuf = 4096;
-constexpr int kStoreBytes = 4 * 2 * kStoreBuf;
+// Staging for the G tile stores: 32 KiB shared by the epilogue warps, i.e.
+// two 32 x 32 buffers per warp for 16-bit G, one for fp32 G.
+constexpr int kStoreBytes = 32768;
 constexpr int kSmemBytes = kStages * (kABytes + kBBytes) + kStoreBytes + 1024 /*align*/ + 256 /*barriers*/;
 // CTA-pair mode (cta_group::2): each CTA holds 128 rows of A and 128 of the
 // 256 B rows per stage (32 KiB), so the ring is 6 stages deep.
@@ -206,7 +207,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull_bar[a], 1);
-      ptx::mbar_init(&tempty_bar[a], 4 * kCG);
+      ptx::mbar_init(&tempty_bar[a], kEpiWarps * kCG);
     }
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -337,6 +338,10 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     // ---------------------------------------------------- epilogue
     const int wq = warp & 3;  // TMEM lane quarter this warp may access
     const int row_t = wq * 32 + lane;
+    const int ew = warp - 2;                        // epilogue warp index
+    const int ch = ew / 4;                          // which half of the 256 columns
+    constexpr int kChunks32 = kBN / 32 / kColHalves;  // 32-column chunks per warp
+    const int c_begin = ch * kChunks32, c_end = c_begin + kChunks32;
     float alpha = 1.0f;
     if constexpr (EPI == EPI_STORE) {
       const float num = ep.alpha_num ? *ep.alpha_num : 1.0f;
@@ -378,7 +383,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         const int tcol = (rel >= 0 && rel < ncols) ? static_cast<int>(rel) : -1;
         float mrun = -INFINITY, srun = 0.0f, tval = 0.0f;
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = c_begin; c < c_end; ++c) {
           if (c * 32 >= ncols) break;
           uint32_t r[32];
           __syncwarp();
@@ -414,8 +419,9 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           }
         }
         if (row_ok) {
-          ep.part[static_cast<int64_t>(nb) * M + row] = make_float2(mrun, srun);
-          if (tcol >= 0) ep.tgt[row] = tval;
+          ep.part[(static_cast<int64_t>(nb) * kColHalves + ch) * M + row] = make_float2(mrun, srun);
+          // Only the warp whose column half holds the label writes the target.
+          if (tcol >= c_begin * 32 && tcol < c_end * 32) ep.tgt[row] = tval;
         }
       } else if constexpr (EPI == EPI_CE_GRAD) {
         const int64_t lab = row_ok ? ep.labels[row] : ep.ignore_index;
@@ -431,10 +437,13 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         constexpr int kRowBytes = 32 * kElem;
         constexpr int kChunks = kRowBytes / 16;
         const int swz = kElem == 2 ? ((lane >> 1) & 3) : (lane & 7);
-        uint8_t* wbuf = sStore + (warp - 2) * 2 * kStoreBuf;
+        constexpr int kBufBytes = 32 * kRowBytes;
+        constexpr int kBufs = kStoreBytes / (kEpiWarps * kBufBytes) >= 2 ? 2 : 1;
+        static_assert(kEpiWarps * kBufs * kBufBytes <= kStoreBytes, "G staging exceeds its shared memory");
+        uint8_t* wbuf = sStore + ew * kBufs * kBufBytes;
         const int store_row0 = mb * kTileM + static_cast<int>(rank) * kBM + rb * kBM + wq * 32;
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = c_begin; c < c_end; ++c) {
           if (c * 32 >= ncols) break;
           uint32_t r[32];
           __syncwarp();
@@ -448,8 +457,8 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             if (j == jt) p -= 1.0f;
             v[j] = p * gs;
           }
-          uint8_t* buf = wbuf + (store_seq & 1) * kStoreBuf;
-          if (store_seq >= 2 && lane == 0) ptx::bulk_wait_read<1>();  // buffer's previous store has read it
+          uint8_t* buf = wbuf + (store_seq % kBufs) * kBufBytes;
+          if (store_seq >= kBufs && lane == 0) ptx::bulk_wait_read<kBufs - 1>();  // buffer's last store has read it
           __syncwarp();
           alignas(16) T vals[32];
 #pragma unroll
@@ -468,7 +477,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         }
       } else {  // EPI_STORE
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = c_begin; c < c_end; ++c) {
           if (c * 32 >= ncols) break;
           uint32_t r[32];
           __syncwarp();
@@ -586,6 +595,7 @@ __global__ void ce_row_reduce_kernel(const float2* __restrict__ part, int n_tile
   float m = -INFINITY, s = 0.0f;
   for (int t = 0; t < n_tiles; ++t) {
     const float2 p = part[static_cast<int64_t>(t) * M + row];
+    if (p.x == -INFINITY) continue;  // a column half with no valid columns
     const float mn = fmaxf(m, p.x);
     s = s * ptx::ex2((m - mn) * kLog2e) + p.y * ptx::ex2((p.x - mn) * kLog2e);
     m = mn;
@@ -740,12 +750,13 @@ const int g_cta_pairs = [] {
   return m == 1 ? 15 : m;
 }();
 // Wide single-CTA 256 x 256 tiles, same bit mask (NIMBLEML_TIED_CE_WIDE).
-// Default 14: the three backward GEMMs use wide tiles (a third fewer operand
-// bytes per FLOP lets them run at higher clocks under the power cap), the
-// forward keeps 128 x 256 tiles whose epilogue overlaps the next tile's MMAs.
+// Default 15, all four GEMMs: a third fewer operand bytes per FLOP lets the
+// step run at higher clocks under the power cap, which outweighs the lost
+// overlap of the epilogue with the next tile's MMAs (the 8 epilogue warps
+// keep that epilogue short).
 const int g_wide = [] {
   const char* v = std::getenv("NIMBLEML_TIED_CE_WIDE");
-  if (!v) return 14;
+  if (!v) return 15;
   const int m = std::atoi(v);
   return m == 1 ? 15 : m;
 }();
@@ -900,9 +911,9 @@ struct FwdLayout {
 };
 FwdLayout fwd_layout(int64_t N, int64_t d, int64_t V, int dtype) {
   FwdLayout L;
-  const int64_t n_tiles = (V + kBN - 1) / kBN;
+  const int64_t n_parts = (V + kBN - 1) / kBN * kColHalves;  // one pair per tile and column half
   size_t off = 0;
-  L.part = off; off = align_up(off + sizeof(float2) * n_tiles * N);
+  L.part = off; off = align_up(off + sizeof(float2) * n_parts * N);
   L.tgt = off; off = align_up(off + sizeof(float) * N);
   if (dtype == NIMBLE_DTYPE_F32) {
     L.hr = off; off = align_up(off + sizeof(float) * N * d);
@@ -1013,9 +1024,9 @@ extern "C" int nimble_tied_ce_forward(const void* hidden, const void* weights, c
   ep.tgt = reinterpret_cast<float*>(ws + L.tgt);
   ep.status = status;
   if (int rc = gemm_dispatch<EPI_CE_FWD>(dtype, A, d_model, B, d_model, n_tokens, v_local, d_model, ep, s)) return rc;
-  const int n_tiles = static_cast<int>((v_local + kBN - 1) / kBN);
+  const int n_parts = static_cast<int>((v_local + kBN - 1) / kBN * kColHalves);
   ce_row_reduce_kernel<<<static_cast<unsigned>((n_tokens + 255) / 256), 256, 0, s>>>(
-      ep.part, n_tiles, ep.tgt, labels, n_tokens, v_offset, v_local, shard_max, shard_sumexp, shard_target);
+      ep.part, n_parts, ep.tgt, labels, n_tokens, v_offset, v_local, shard_max, shard_sumexp, shard_target);
   NIMBLE_CUDA_TRY(cudaGetLastError());
   return NIMBLE_OK;
 }
