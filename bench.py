@@ -531,7 +531,7 @@ def main():
                    "l2": "inputs larger than L2 (h %.0f MB, E %.0f MB), no flush" % (
                        n * d * h.element_size() / 1e6, v * d * h.element_size() / 1e6),
                    "backward_slabs": n_slabs},
-        "roofline": {"bound": "tensor", "kernel": "tc_gemm_tn_kernel<EPI_CE_FWD> (+ row reduce)",
+        "roofline": {"bound": "tensor", "kernel": "tc_gemm_tn_kernel<EPI_CE_FWD>, wide 256x256 tiles (+ row reduce)",
                      "achieved": fwd_tflops, "peak": sustained, "unit": "TFLOP/s",
                      "frac": fwd_tflops / sustained, "peak_kind": f"{peak_kind} sustained bf16 cuBLAS",
                      "traffic": traffic, "flops_per_launch": flops_fwd_launch,
