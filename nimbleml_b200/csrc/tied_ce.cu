@@ -765,11 +765,11 @@ template <int EPI, bool kAMN>
 constexpr int gemm_kind_bit() {
   return EPI == EPI_CE_FWD ? 1 : EPI == EPI_CE_GRAD ? 2 : kAMN ? 4 : 8;
 }
-// Token blocks per rasterisation group (NIMBLEML_TIED_CE_GROUP_M, default 16).
+// Token blocks per rasterisation group (NIMBLEML_TIED_CE_GROUP_M, default 8: 2048 token rows with 256-row wide tiles).
 const int g_group_m = [] {
   const char* v = std::getenv("NIMBLEML_TIED_CE_GROUP_M");
   const int g = v ? std::atoi(v) : 0;
-  return g > 0 ? g : 16;
+  return g > 0 ? g : 8;
 }();
 
 // Row-major [rows x cols] output written by 32 x 32 TMA box stores from a
