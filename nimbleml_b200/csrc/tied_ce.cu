@@ -1036,7 +1036,8 @@ extern "C" int nimble_tied_ce_combine(const float* shard_max, const float* shard
                                       int64_t ignore_index, float* out_max, float* out_sumexp, float* out_lse,
                                       float* out_loss, float* out_valid_count, int* status, void* stream) {
   if (n_shards <= 0 || n_tokens < 0 || vocab_size <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "bad sizes");
-  if (!out_lse || !out_loss || !out_valid_count) return fail(NIMBLE_ERR_INVALID_ARG, "null output pointer");
+  if (!out_loss || !out_valid_count || (n_tokens > 0 && !out_lse))
+    return fail(NIMBLE_ERR_INVALID_ARG, "null output pointer");
   if (n_tokens > 0 && (!shard_max || !shard_sumexp || !shard_target || !labels))
     return fail(NIMBLE_ERR_INVALID_ARG, "null input pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1063,7 +1064,7 @@ int backward_impl(const float* grad_scale, const void* hidden, const void* weigh
                   void* workspace, size_t workspace_bytes, int* status, void* stream, void* dh_done_event,
                   int last_de_max_ctas) {
   if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype)) return rc;
-  if (!grad_hidden || !grad_weights || !grad_scale || !lse || !valid_count)
+  if (!grad_weights || !grad_scale || !valid_count || (n_tokens > 0 && (!grad_hidden || !lse)))
     return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
   for (int dt : {grad_hidden_dtype, grad_weights_dtype})
     if (dt != NIMBLE_DTYPE_F32 && dt != NIMBLE_DTYPE_F16 && dt != NIMBLE_DTYPE_BF16)

@@ -304,3 +304,28 @@ def test_overlap_entry_point_matches_backward():
     torch.cuda.synchronize()
     assert ev.query()
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+def test_empty_batch():
+    """No tokens: loss 0 with no valid rows, an all-zero tied grad, an empty hidden grad
+    (the reference divides 0 by 0 here; this path returns the defined 0)."""
+    from nimbleml_b200.kernels import fused_tied_crossentropy as k
+    from nimbleml_b200.losses import CrossEntropyLoss
+
+    e = to_dev(np.random.default_rng(0).standard_normal((100, 64)) * 0.02, torch.float16)
+    h = torch.empty((0, 64), dtype=torch.float16, device="cuda")
+    y = torch.empty((0,), dtype=torch.int64, device="cuda")
+    loss, hh, ww, st, mx, se = k.fused_tied_crossentropy_forward(h, e, y)
+    dh, de = k.fused_tied_crossentropy_backward(1.0, hh, ww, y, st, mx, se)
+    torch.cuda.synchronize()
+    assert float(loss) == 0.0 and float(st.valid_count) == 0.0
+    assert dh.shape == (0, 64) and de.shape == (100, 64) and not de.any()
+    hid = torch.empty((0, 4, 64), dtype=torch.float16, device="cuda", requires_grad=True)
+    emb = e.clone().requires_grad_(True)
+    out = CrossEntropyLoss().forward_tied(hid, emb, torch.empty((0, 4), dtype=torch.int64, device="cuda"))
+    out.backward()
+    assert float(out) == 0.0 and not emb.grad.any() and hid.grad.shape == (0, 4, 64)
+    lg = torch.empty((0, 10), dtype=torch.float16, device="cuda", requires_grad=True)
+    l2 = CrossEntropyLoss()(lg, torch.empty((0,), dtype=torch.int64, device="cuda"))
+    l2.backward()
+    assert float(l2) == 0.0 and lg.grad.shape == (0, 10)
