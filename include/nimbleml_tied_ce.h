@@ -48,7 +48,12 @@ extern "C" {
 enum {
   NIMBLE_DTYPE_F32 = 0,  /* fp32 storage, tcgen05 kind::tf32 with RN rounding */
   NIMBLE_DTYPE_F16 = 1,  /* fp16, tcgen05 kind::f16, fp32 accumulate        */
-  NIMBLE_DTYPE_BF16 = 2  /* bf16, tcgen05 kind::f16, fp32 accumulate        */
+  NIMBLE_DTYPE_BF16 = 2, /* bf16, tcgen05 kind::f16, fp32 accumulate        */
+  /* fp32 storage whose values are already TF32 (rounded by nimble_round_tf32).
+   * Accepted as the compute dtype of the tied-CE forward / backward only:
+   * they then read hidden / weights in place instead of making rounded
+   * copies, so a caller rounds once per forward + backward pair. */
+  NIMBLE_DTYPE_TF32 = 3
 };
 
 /* Return codes. Device-side conditions are reported through `status`. */
@@ -155,6 +160,23 @@ NIMBLE_API int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
                             int grad_hidden_dtype, void* grad_weights, int grad_weights_dtype,
                             int accumulate_grad_weights, size_t slab_bytes, void* workspace,
                             size_t workspace_bytes, int* status, void* stream);
+
+/* Bytes of workspace nimble_tied_ce_backward_overlap needs. That entry point
+ * serves a shard of a vocabulary split over P >= 2 ranks (at most half of
+ * the vocabulary), so its slabs follow the slab_bytes budget alone: a shard
+ * whose G fits the budget is walked in one slab, with no fp32 grad_hidden
+ * accumulator. No counterpart in the reference (no multi-GPU path). */
+NIMBLE_API int nimble_tied_ce_backward_overlap_workspace_size(int64_t n_tokens, int64_t d_model,
+                                                              int64_t v_local, int dtype,
+                                                              size_t slab_bytes, size_t* bytes);
+
+/* dst[i] = src[i] rounded to the nearest TF32 value (ties away from zero,
+ * cvt.rna.tf32.f32), in fp32 storage. A caller that passes the rounded
+ * copies of hidden and weights with dtype NIMBLE_DTYPE_TF32 to the tied-CE
+ * forward and backward rounds once per pair instead of once per call. Plays
+ * the part of the reference's fp32 on_device copy
+ * (NimbleML/utils/np_backend.py:184-190) for the TF32 tensor cores. */
+NIMBLE_API int nimble_round_tf32(const float* src, float* dst, int64_t n, void* stream);
 
 /* Diagnostic for the failure path (no counterpart in the reference, which has
  * no device-side waits): launches one block whose bounded mbarrier wait —
@@ -289,8 +311,10 @@ NIMBLE_API int nimble_adamw_step(float* weights, const void* grad, int grad_dtyp
  * 64 MiB array inside this library, resident on every GPU that loads it until
  * the process exits. Sizes whose forward workspace
  * (nimble_tied_ce_forward_workspace_size) exceeds 64 MiB are rejected with
- * NIMBLE_ERR_INVALID_ARG. Calls no cudaMalloc / cudaFree. The first call on
- * each device looks up the array's device address, so make it before any
+ * NIMBLE_ERR_INVALID_ARG. Calls no cudaMalloc / cudaFree. Every call looks
+ * up the array's device address on the current device (cudaGetSymbolAddress,
+ * no allocation), so the address stays valid after cudaDeviceReset; the
+ * first call on a device may load the module there, so make it before any
  * stream capture. All calls share the one array: calls that overlap on the
  * GPU (different streams, or different host threads on one device) race and
  * must be serialised by the caller. Results equal nimble_tied_ce_forward's. */

@@ -24,6 +24,7 @@ _INSTALL_HINT = (
 DTYPE_F32 = 0
 DTYPE_F16 = 1
 DTYPE_BF16 = 2
+DTYPE_TF32 = 3  # fp32 storage already rounded to TF32 (nimble_round_tf32)
 
 STATUS_BAD_LABEL = 1
 STATUS_WAIT_TIMEOUT = 2
@@ -53,6 +54,9 @@ SIGNATURES = {
          _c_vp, _c_vp, _c_vp, _c_vp]),
     "nimble_tied_ce_backward_workspace_size": (
         _c_int, [_c_i64, _c_i64, _c_i64, _c_int, _c_size, ctypes.POINTER(_c_size)]),
+    "nimble_tied_ce_backward_overlap_workspace_size": (
+        _c_int, [_c_i64, _c_i64, _c_i64, _c_int, _c_size, ctypes.POINTER(_c_size)]),
+    "nimble_round_tf32": (_c_int, [_c_vp, _c_vp, _c_i64, _c_vp]),
     "nimble_tied_ce_probe_wait_timeout": (_c_int, [ctypes.c_uint64, _c_vp, _c_vp]),
     "nimble_tied_logits_forward": (
         _c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_i64, _c_int, _c_vp]),
@@ -129,10 +133,10 @@ class NativeLibrary:
         self.call("nimble_tied_ce_forward_workspace_size", n, d, v_local, dtype, ctypes.byref(out))
         return out.value
 
-    def backward_workspace_size(self, n, d, v_local, dtype, slab_bytes=0) -> int:
+    def backward_workspace_size(self, n, d, v_local, dtype, slab_bytes=0, overlap=False) -> int:
         out = _c_size(0)
-        self.call("nimble_tied_ce_backward_workspace_size", n, d, v_local, dtype, slab_bytes,
-                  ctypes.byref(out))
+        name = "nimble_tied_ce_backward_overlap_workspace_size" if overlap else "nimble_tied_ce_backward_workspace_size"
+        self.call(name, n, d, v_local, dtype, slab_bytes, ctypes.byref(out))
         return out.value
 
     def rmsnorm_backward_workspace_size(self, n, d) -> int:
@@ -153,4 +157,4 @@ def load_native() -> NativeLibrary:
 native = load_native()
 
 __all__ = ["native", "load_native", "NativeLibrary", "SIGNATURES", "DTYPE_F32", "DTYPE_F16",
-           "DTYPE_BF16", "STATUS_BAD_LABEL", "STATUS_WAIT_TIMEOUT"]
+           "DTYPE_BF16", "DTYPE_TF32", "STATUS_BAD_LABEL", "STATUS_WAIT_TIMEOUT"]

@@ -13,7 +13,7 @@ namespace nimble {
 // nimble_tied_ce_last_error) and returns `code`.
 int fail(int code, const std::string& msg);
 
-inline int elem_size(int dtype) { return dtype == NIMBLE_DTYPE_F32 ? 4 : 2; }
+inline int elem_size(int dtype) { return (dtype == NIMBLE_DTYPE_F32 || dtype == NIMBLE_DTYPE_TF32) ? 4 : 2; }
 
 inline bool valid_dtype(int dtype) {
   return dtype == NIMBLE_DTYPE_F32 || dtype == NIMBLE_DTYPE_F16 || dtype == NIMBLE_DTYPE_BF16;

@@ -144,9 +144,11 @@ __device__ __forceinline__ void store_out_elem(void* p, int64_t i, int dt, float
 
 // ------------------------------------------------------------- the GEMM
 // Persistent, warp-specialised: warp 0 lane 0 issues TMA loads into a
-// kStages ring, warp 1 lane 0 issues tcgen05.mma into one of two TMEM
-// accumulators, warps 2-5 (one thread per accumulator row) run the epilogue
-// of tile i while the MMAs of tile i+1 proceed. kAMN / kBMN select an
+// shared-memory ring, warp 1 lane 0 issues tcgen05.mma into TMEM, and warps
+// 2-9 run the epilogue (two warps per TMEM lane quarter, each on half of the
+// 256 columns, one thread per accumulator row). With 128 x 256 tiles the two
+// TMEM accumulators alternate, so the epilogue of tile i overlaps the MMAs of
+// tile i+1. kAMN / kBMN select an
 // MN-major A / B operand (the tensor map's inner dimension is then M / N and
 // the tile arrives as 128-byte-wide MN chunks of K rows).
 //
@@ -643,7 +645,9 @@ ce_combine_kernel(const float* __restrict__ smax, const float* __restrict__ ssum
   s_loss[threadIdx.x] = acc;
   s_cnt[threadIdx.x] = cnt;
   if (bad && status) atomicOr(status, NIMBLE_STATUS_BAD_LABEL);
-  __syncthreads();
+  // A label outside [0, V) makes the loss NaN: the caller sees it without a
+  // host read of the status word (the reference raises IndexError there).
+  const int any_bad = __syncthreads_or(bad);
   for (int w = kCombineThreads / 2; w > 0; w >>= 1) {
     if (threadIdx.x < w) {
       s_loss[threadIdx.x] += s_loss[threadIdx.x + w];
@@ -653,7 +657,7 @@ ce_combine_kernel(const float* __restrict__ smax, const float* __restrict__ ssum
   }
   if (threadIdx.x == 0) {
     const int n = s_cnt[0];
-    out_loss[0] = n > 0 ? static_cast<float>(s_loss[0] / n) : 0.0f;
+    out_loss[0] = any_bad ? __int_as_float(0x7fc00000) : (n > 0 ? static_cast<float>(s_loss[0] / n) : 0.0f);
     out_valid[0] = static_cast<float>(n);
   }
 }
@@ -735,8 +739,9 @@ int make_operand_map(CUtensorMap* map, const void* base, int dtype, bool mn_majo
   return NIMBLE_OK;
 }
 
-// GEMM tiling mode. One CTA per 128 x 256 tile by default; CTA pairs
-// (cta_group::2, 256 x 256 tiles) with NIMBLEML_TIED_CE_CTA_PAIRS=1. The pair
+// GEMM tiling mode per GEMM kind: wide single-CTA 256 x 256 tiles by default
+// (g_wide below), 128 x 256 tiles per CTA when a kind's wide bit is cleared,
+// CTA pairs (cta_group::2, 256 x 256 tiles) with NIMBLEML_TIED_CE_CTA_PAIRS. The pair
 // kernel keeps the tensor pipe busier per clock but draws more energy per
 // FLOP, so under the B200's 1 kW cap it runs at lower clocks and is slower
 // over a whole fwd+bwd step.
@@ -915,7 +920,7 @@ FwdLayout fwd_layout(int64_t N, int64_t d, int64_t V, int dtype) {
   size_t off = 0;
   L.part = off; off = align_up(off + sizeof(float2) * n_parts * N);
   L.tgt = off; off = align_up(off + sizeof(float) * N);
-  if (dtype == NIMBLE_DTYPE_F32) {
+  if (dtype == NIMBLE_DTYPE_F32) {  // NIMBLE_DTYPE_TF32 inputs are used in place
     L.hr = off; off = align_up(off + sizeof(float) * N * d);
     L.er = off; off = align_up(off + sizeof(float) * V * d);
   }
@@ -931,21 +936,25 @@ struct BwdLayout {
   int64_t slab = 0, n_slabs = 0;
   size_t g = 0, dh = 0, hr = 0, er = 0, total = 0;
 };
-BwdLayout bwd_layout(int64_t N, int64_t d, int64_t V, int dtype, size_t slab_bytes) {
+// `whole_vocab`: the shard may be the entire vocabulary (one GPU), so the
+// backward walks it in at least two slabs and no G buffer ever holds more
+// than half of the N x V logits. A shard of a vocabulary split over P >= 2
+// ranks is at most half of it already; its slabs follow the byte budget
+// alone, so a shard whose G fits the budget is one slab and needs no fp32
+// grad_hidden accumulator.
+BwdLayout bwd_layout(int64_t N, int64_t d, int64_t V, int dtype, size_t slab_bytes, bool whole_vocab = true) {
   BwdLayout L;
   const int64_t es = elem_size(dtype);
   if (slab_bytes == 0) slab_bytes = kDefaultSlabBytes;
   int64_t cols = static_cast<int64_t>(slab_bytes / (es * std::max<int64_t>(N, 1)));
   cols = std::max<int64_t>(kBN, cols / kBN * kBN);
-  // At least two slabs: the G slab never holds more than half of the shard's
-  // N x V_local logits, however large the budget.
-  cols = std::min<int64_t>(cols, round_up((V + 1) / 2, kBN));
+  cols = std::min<int64_t>(cols, whole_vocab ? round_up((V + 1) / 2, kBN) : round_up(V, kBN));
   L.slab = cols;
   L.n_slabs = (V + cols - 1) / cols;
   size_t off = 0;
   L.g = off; off = align_up(off + es * N * cols);
   if (L.n_slabs > 1) { L.dh = off; off = align_up(off + sizeof(float) * N * d); }
-  if (dtype == NIMBLE_DTYPE_F32) {
+  if (dtype == NIMBLE_DTYPE_F32) {  // NIMBLE_DTYPE_TF32 inputs are used in place
     L.hr = off; off = align_up(off + sizeof(float) * N * d);
     L.er = off; off = align_up(off + sizeof(float) * V * d);
   }
@@ -956,9 +965,11 @@ BwdLayout bwd_layout(int64_t N, int64_t d, int64_t V, int dtype, size_t slab_byt
 // Shape / dtype / pointer checks shared by the entry points; `labels` may be
 // null when the entry point takes none (the tied-logits GEMMs).
 int check_common(const void* h, const void* w, const int64_t* labels, int64_t N, int64_t d, int64_t V, int dtype,
-                 bool needs_labels = true) {
-  if (dtype != NIMBLE_DTYPE_F32 && dtype != NIMBLE_DTYPE_F16 && dtype != NIMBLE_DTYPE_BF16)
-    return fail(NIMBLE_ERR_INVALID_ARG, "dtype must be NIMBLE_DTYPE_F32, F16 or BF16");
+                 bool needs_labels = true, bool allow_tf32 = false) {
+  if (dtype != NIMBLE_DTYPE_F32 && dtype != NIMBLE_DTYPE_F16 && dtype != NIMBLE_DTYPE_BF16 &&
+      !(allow_tf32 && dtype == NIMBLE_DTYPE_TF32))
+    return fail(NIMBLE_ERR_INVALID_ARG, allow_tf32 ? "dtype must be NIMBLE_DTYPE_F32, F16, BF16 or TF32"
+                                                   : "dtype must be NIMBLE_DTYPE_F32, F16 or BF16");
   if (N < 0 || d <= 0 || V <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "sizes must be positive");
   if ((d * elem_size(dtype)) % 16 != 0)
     return fail(NIMBLE_ERR_INVALID_ARG, "d_model * element size must be a multiple of 16 bytes");
@@ -1000,7 +1011,7 @@ extern "C" int nimble_tied_ce_forward(const void* hidden, const void* weights, c
                                       int64_t d_model, int64_t v_local, int64_t v_offset, int dtype, float* shard_max,
                                       float* shard_sumexp, float* shard_target, void* workspace,
                                       size_t workspace_bytes, int* status, void* stream) {
-  if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype)) return rc;
+  if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype, true, true)) return rc;
   if (n_tokens == 0) return NIMBLE_OK;
   if (!shard_max || !shard_sumexp || !shard_target) return fail(NIMBLE_ERR_INVALID_ARG, "null output pointer");
   const FwdLayout L = fwd_layout(n_tokens, d_model, v_local, dtype);
@@ -1017,6 +1028,7 @@ extern "C" int nimble_tied_ce_forward(const void* hidden, const void* weights, c
     A = hr;
     B = er;
   }
+  if (dtype == NIMBLE_DTYPE_TF32) dtype = NIMBLE_DTYPE_F32;  // already rounded: read in place
   EpiParams ep{};
   ep.labels = labels;
   ep.col_origin = v_offset;
@@ -1056,6 +1068,20 @@ extern "C" int nimble_tied_ce_backward_workspace_size(int64_t n_tokens, int64_t 
   return NIMBLE_OK;
 }
 
+extern "C" int nimble_tied_ce_backward_overlap_workspace_size(int64_t n_tokens, int64_t d_model, int64_t v_local,
+                                                              int dtype, size_t slab_bytes, size_t* bytes) {
+  if (!bytes) return fail(NIMBLE_ERR_INVALID_ARG, "bytes is null");
+  if (n_tokens < 0 || d_model <= 0 || v_local <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "sizes must be positive");
+  *bytes = bwd_layout(n_tokens, d_model, v_local, dtype, slab_bytes, /*whole_vocab=*/false).total;
+  return NIMBLE_OK;
+}
+
+extern "C" int nimble_round_tf32(const float* src, float* dst, int64_t n, void* stream) {
+  if (n < 0) return fail(NIMBLE_ERR_INVALID_ARG, "n must be >= 0");
+  if (n > 0 && (!src || !dst)) return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  return launch_round(src, dst, n, static_cast<cudaStream_t>(stream));
+}
+
 namespace {
 int backward_impl(const float* grad_scale, const void* hidden, const void* weights, const int64_t* labels,
                   const float* lse, const float* valid_count, int64_t n_tokens, int64_t d_model, int64_t v_local,
@@ -1063,7 +1089,7 @@ int backward_impl(const float* grad_scale, const void* hidden, const void* weigh
                   void* grad_weights, int grad_weights_dtype, int accumulate_grad_weights, size_t slab_bytes,
                   void* workspace, size_t workspace_bytes, int* status, void* stream, void* dh_done_event,
                   int last_de_max_ctas) {
-  if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype)) return rc;
+  if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype, true, true)) return rc;
   if (!grad_weights || !grad_scale || !valid_count || (n_tokens > 0 && (!grad_hidden || !lse)))
     return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
   for (int dt : {grad_hidden_dtype, grad_weights_dtype})
@@ -1079,7 +1105,7 @@ int backward_impl(const float* grad_scale, const void* hidden, const void* weigh
       NIMBLE_CUDA_TRY(cudaMemsetAsync(grad_weights, 0, elem_size(grad_weights_dtype) * v_local * d_model, s));
     return NIMBLE_OK;
   }
-  const BwdLayout L = bwd_layout(n_tokens, d_model, v_local, dtype, slab_bytes);
+  const BwdLayout L = bwd_layout(n_tokens, d_model, v_local, dtype, slab_bytes, /*whole_vocab=*/!dh_done_event);
   if (!workspace || workspace_bytes < L.total) return fail(NIMBLE_ERR_WORKSPACE, "backward workspace too small");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const int64_t es = elem_size(dtype);
@@ -1093,6 +1119,7 @@ int backward_impl(const float* grad_scale, const void* hidden, const void* weigh
     h = hr;
     E = er;
   }
+  if (dtype == NIMBLE_DTYPE_TF32) dtype = NIMBLE_DTYPE_F32;  // already rounded: read in place
   void* g = ws + L.g;
   float* dh_acc = L.n_slabs > 1 ? reinterpret_cast<float*>(ws + L.dh) : nullptr;
 
@@ -1315,24 +1342,15 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;  // 64 MiB
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[kMaxDevices] = {};
-
 // Device address of the scratch array on the current device. In host code
-// the symbol is only a host-side stand-in, so the address must be looked up
-// once per device with that device current.
+// the symbol is only a host-side stand-in, so the address is looked up with
+// the device current. It is looked up on every call (no allocation, no
+// cached pointer), so it stays right after cudaDeviceReset or a reload of
+// the module.
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  NIMBLE_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kMaxDevices) return fail(NIMBLE_ERR_UNSUPPORTED, "device index out of range");
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    NIMBLE_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  NIMBLE_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+  *out = p;
   return NIMBLE_OK;
 }
 
@@ -1343,7 +1361,7 @@ extern "C" int nimble_tied_ce_forward_noalloc(const void* hidden, const void* we
                                               int64_t n_tokens, int64_t d_model, int64_t v_local,
                                               int64_t v_offset, int dtype, float* shard_max, float* shard_sumexp,
                                               float* shard_target, int* status, void* stream) {
-  if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype)) return rc;
+  if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype, true, true)) return rc;
   const size_t need = fwd_layout(n_tokens, d_model, v_local, dtype).total;
   if (need > kNoAllocScratchBytes)
     return fail(NIMBLE_ERR_INVALID_ARG,

@@ -22,6 +22,15 @@ Inputs are torch CUDA tensors (or anything ``torch.as_tensor`` accepts; host
 arrays are copied to the current device). On a CUDA device every launch goes
 through ``libnimbleml_tied_ce.so``; there is no CPU or library fallback, and a
 missing library raises at import.
+
+Device-side errors (a label outside [0, V), a bounded device wait that gave
+up) are OR-ed into a per-device status word. Without any host sync, a label
+error makes the loss NaN at once, and every call of the path first reads an
+asynchronous pinned-memory copy of the word taken at the end of an earlier
+call, raising if a bit is set. So an error raises at the latest a few calls
+later; results of a call are undefined until a later check has passed.
+``check_status`` reads the word synchronously (``NIMBLEML_CHECK_BOUNDS=1``
+does that after every call).
 """
 from __future__ import annotations
 
@@ -35,6 +44,7 @@ from nimbleml_b200._native_loader import (
     DTYPE_BF16,
     DTYPE_F16,
     DTYPE_F32,
+    DTYPE_TF32,
     STATUS_BAD_LABEL,
     STATUS_WAIT_TIMEOUT,
     native,
@@ -59,6 +69,9 @@ class TiedCEStats:
     ignore_index: int          # rows with this label contribute nothing
     vocab_size: int            # total vocabulary V
     vocab_offset: int = 0      # first global class id of the local weight shard
+    # fp32 only: TF32-rounded copies of (hidden, weights) made by the forward,
+    # reused by the backward so each pair of calls rounds once.
+    rounded: Optional[tuple] = None
 
 
 _status_words: dict = {}
@@ -74,17 +87,81 @@ def status_word(device: torch.device) -> torch.Tensor:
     return buf
 
 
+def _raise_for(val: int) -> None:
+    if val & STATUS_WAIT_TIMEOUT:
+        raise RuntimeError("tied-CE kernel aborted: a bounded device wait timed out; "
+                           "the outputs of the calls since the last check are undefined")
+    if val & STATUS_BAD_LABEL:
+        raise ValueError("label index out of range for the vocabulary")
+
+
 def check_status(device: torch.device, *, clear: bool = True) -> int:
     """Reads (host sync) and optionally clears the device status word; raises on error bits."""
     buf = status_word(device)
     val = int(buf.item())
     if clear and val:
         buf.zero_()
-    if val & STATUS_WAIT_TIMEOUT:
-        raise RuntimeError("tied-CE kernel aborted: a bounded device wait timed out")
-    if val & STATUS_BAD_LABEL:
-        raise ValueError("label index out of range for the vocabulary")
+    _raise_for(val)
     return val
+
+
+class _StatusMonitor:
+    """Asynchronous reads of one device's status word (no host sync).
+
+    ``snapshot`` enqueues a copy of the word into pinned host memory on the
+    current stream and records an event; ``poll`` looks at the copy only once
+    that event has completed (``Event.query`` does not block), and raises
+    (clearing the device word) when an error bit is set.
+    """
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = torch.cuda.Event()
+        self.pending = False
+
+    def snapshot(self) -> None:
+        self.host.copy_(status_word(self.device), non_blocking=True)
+        self.event.record(torch.cuda.current_stream(self.device))
+        self.pending = True
+
+    def poll(self) -> None:
+        if not self.pending or not self.event.query():
+            return
+        self.pending = False
+        val = int(self.host[0])
+        if val:
+            status_word(self.device).zero_()
+            _raise_for(val)
+
+
+_monitors: dict = {}
+
+
+def _monitor(device: torch.device) -> _StatusMonitor:
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    mon = _monitors.get(key)
+    if mon is None:
+        mon = _StatusMonitor(torch.device("cuda", key))
+        _monitors[key] = mon
+    return mon
+
+
+def poll_status(device: torch.device) -> None:
+    """Raises if an earlier call's status copy, already on the host, shows an error."""
+    _monitor(device).poll()
+
+
+def snapshot_status(device: torch.device) -> None:
+    """Enqueues the asynchronous host copy of the status word read by poll_status."""
+    _monitor(device).snapshot()
+
+
+def round_tf32(x: torch.Tensor) -> torch.Tensor:
+    """A TF32-rounded fp32 copy of ``x`` (nimble_round_tf32 on the device)."""
+    out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    native.call("nimble_round_tf32", x.data_ptr(), out.data_ptr(), x.numel(), _stream_ptr(x.device))
+    return out
 
 
 def _stream_ptr(device: torch.device) -> int:
@@ -124,15 +201,21 @@ def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
 
-def shard_forward(h: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, vocab_offset: int = 0):
+def shard_forward(h: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, vocab_offset: int = 0, *,
+                  rounded: bool = False):
     """Per-token (max, sum-exp, target) over the columns of one weight shard.
 
     Returns a (3, N) fp32 tensor: rows are shard max, shard sum-exp and the
-    target logit (0 where the label lies outside the shard).
+    target logit (0 where the label lies outside the shard). ``rounded``: fp32
+    ``h`` and ``w`` already hold TF32 values (``round_tf32``) and are read in
+    place.
     """
     n, d = h.shape
     v_local = w.shape[0]
     dt = compute_dtype_of(h)
+    if rounded and dt == DTYPE_F32:
+        dt = DTYPE_TF32
+    poll_status(h.device)
     out = torch.empty((3, n), dtype=torch.float32, device=h.device)
     ws = _workspace(native.forward_workspace_size(n, d, v_local, dt), h.device)
     native.call(
@@ -156,6 +239,7 @@ def combine(shard_stats: torch.Tensor, labels: torch.Tensor, vocab_size: int, ig
         labels.data_ptr(), n, vocab_size, ignore_index, gmax.data_ptr(), gsum.data_ptr(),
         lse.data_ptr(), scalars[0:1].data_ptr(), scalars[1:2].data_ptr(),
         status_word(dev).data_ptr(), _stream_ptr(dev))
+    snapshot_status(dev)
     return gmax, gsum, lse, scalars[0], scalars[1:2]
 
 
@@ -175,13 +259,17 @@ def shard_backward(grad_scale: torch.Tensor, h: torch.Tensor, w: torch.Tensor, l
     v_local = w.shape[0]
     dt = compute_dtype_of(h)
     dev = h.device
+    poll_status(dev)
+    if stats.rounded is not None and dt == DTYPE_F32:
+        h, w = stats.rounded  # the forward's TF32 copies: no second rounding pass
+        dt = DTYPE_TF32
     gh_dtype = grad_hidden_dtype or h.dtype
     grad_h = torch.empty((n, d), dtype=gh_dtype, device=dev)
     if grad_weights is None:
         grad_weights = torch.empty((v_local, d), dtype=h.dtype, device=dev)
         accumulate = False
     slab = SLAB_BYTES if slab_bytes is None else int(slab_bytes)
-    ws = _workspace(native.backward_workspace_size(n, d, v_local, dt, slab), dev)
+    ws = _workspace(native.backward_workspace_size(n, d, v_local, dt, slab, overlap=ready_event is not None), dev)
     gs = grad_scale.reshape(-1)[:1].to(device=dev, dtype=torch.float32).contiguous()
     args = (gs.data_ptr(), h.data_ptr(), w.data_ptr(), labels.data_ptr(), stats.lse.data_ptr(),
             stats.valid_count.data_ptr(), n, d, v_local, stats.vocab_offset, stats.ignore_index, dt,
@@ -192,6 +280,7 @@ def shard_backward(grad_scale: torch.Tensor, h: torch.Tensor, w: torch.Tensor, l
         native.call("nimble_tied_ce_backward", *args)
     else:
         native.call("nimble_tied_ce_backward_overlap", *args, ready_event.cuda_event, int(last_de_max_ctas))
+    snapshot_status(dev)
     return grad_h, grad_weights
 
 
@@ -221,11 +310,12 @@ def fused_tied_crossentropy_forward(hidden, weights, label_indices, *, ignore_in
     n = h.shape[0]
     labels = as_label_indices(label_indices, batch_size=n, device=h.device)
     ign = _NO_IGNORE if ignore_index is None else int(ignore_index)
-    part = shard_forward(h, w, labels)
+    rounded = (round_tf32(h), round_tf32(w)) if h.dtype == torch.float32 else None
+    part = shard_forward(*(rounded or (h, w)), labels, rounded=rounded is not None)
     gmax, gsum, lse, loss, valid = combine(part.unsqueeze(1), labels, w.shape[0], ign)
     if CHECK_BOUNDS:
         check_status(h.device)
-    stats = TiedCEStats(lse=lse, valid_count=valid, ignore_index=ign, vocab_size=w.shape[0])
+    stats = TiedCEStats(lse=lse, valid_count=valid, ignore_index=ign, vocab_size=w.shape[0], rounded=rounded)
     return loss, h, w, stats, gmax.view(n, 1), gsum.view(n, 1)
 
 

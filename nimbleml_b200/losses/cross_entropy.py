@@ -36,6 +36,7 @@ from nimbleml_b200.kernels.fused_tied_crossentropy import (
     check_status,
     combine,
     compute_dtype_of,
+    round_tf32,
     shard_backward,
     shard_forward,
 )
@@ -53,12 +54,14 @@ class _TiedCrossEntropy(torch.autograd.Function):
         if weights.dtype != h2d.dtype:
             weights = weights.to(h2d.dtype)
         weights = weights.contiguous()
-        part = shard_forward(h2d, weights, labels, vocab_offset)
+        rounded = (round_tf32(h2d), round_tf32(weights)) if h2d.dtype == torch.float32 else None
+        part = shard_forward(*(rounded or (h2d, weights)), labels, vocab_offset, rounded=rounded is not None)
         stats3 = vocab_parallel.gather_shard_stats(part, group)  # (3, P, N)
         _, _, lse, loss, valid = combine(stats3, labels, vocab_size, ignore_index)
         if CHECK_BOUNDS:
             check_status(h2d.device)
         ctx.save_for_backward(h2d, weights, labels, lse, valid)
+        ctx.rounded = rounded
         ctx.meta = (ignore_index, vocab_offset, vocab_size, group, weights_in_dtype)
         return loss
 
@@ -69,7 +72,8 @@ class _TiedCrossEntropy(torch.autograd.Function):
         h2d, weights, labels, lse, valid = ctx.saved_tensors
         ignore_index, vocab_offset, vocab_size, group, w_dtype = ctx.meta
         stats = TiedCEStats(lse=lse, valid_count=valid, ignore_index=ignore_index,
-                            vocab_size=vocab_size, vocab_offset=vocab_offset)
+                            vocab_size=vocab_size, vocab_offset=vocab_offset, rounded=ctx.rounded)
+        ctx.rounded = None
         sharded = vocab_parallel.world_size(group) > 1
         grad_w = torch.empty(weights.shape, dtype=w_dtype, device=weights.device)
         if sharded:

@@ -130,18 +130,25 @@ class VocabParallelTiedHead:
         """Replicates host-resident hidden states (N, d) on every rank's GPU.
 
         Each rank copies only its 1/P slice of the rows from host memory
-        (pinned for an asynchronous copy) and one all_gather over NVLink
-        assembles the rest, so PCIe traffic per rank falls from N*d to
-        N*d/P elements. Returns a device tensor (not a leaf of any graph).
+        and one all_gather over NVLink assembles the rest, so PCIe traffic
+        per rank falls from N*d to N*d/P elements. The copy is asynchronous
+        when ``hidden_host`` is pinned; a pageable tensor's slice is pinned
+        here first (one extra host copy of the slice). Returns a device
+        tensor (not a leaf of any graph).
         """
+        dev = self.weights.device
+        pin = dev.type == "cuda"  # pinned memory needs a CUDA driver
         if self.world == 1:
-            return hidden_host.to(self.weights.device, non_blocking=True)
+            src = hidden_host.pin_memory() if pin and not hidden_host.is_pinned() else hidden_host
+            return src.to(dev, non_blocking=True)
         n, d = hidden_host.shape
         per = -(-n // self.world)
         lo, hi = min(self.rank * per, n), min((self.rank + 1) * per, n)
-        dev = self.weights.device
+        rows = hidden_host[lo:hi]
+        if pin and not rows.is_pinned():
+            rows = rows.pin_memory()
         chunk = torch.zeros((per, d), dtype=hidden_host.dtype, device=dev)
-        chunk[: hi - lo].copy_(hidden_host[lo:hi], non_blocking=True)
+        chunk[: hi - lo].copy_(rows, non_blocking=True)
         full = torch.empty((per * self.world, d), dtype=hidden_host.dtype, device=dev)
         dist.all_gather_into_tensor(full, chunk, group=self.group)
         return full[:n]
