@@ -131,14 +131,59 @@ def _dist_setup(gpus):
     return rank, local, world
 
 
+# Upstream grad of the loss for the fp16 backward: 2^15, a dynamic loss
+# scaler's settled scale (2^16 times the upstream grad of an fp16 loss
+# overflows). Unscaled fp16 grads at N = 32768 would fall among fp16
+# subnormals; tests/test_tied_ce_gpu.py pins this exact configuration.
+GRAD_SCALE = {"float16": 32768.0, "bfloat16": 1.0, "float32": 1.0}
+
+
+def all_host_threads():
+    """Lets NumPy's BLAS use every host core the process may run on.
+
+    torchrun exports OMP_NUM_THREADS=1 to every rank; OpenBLAS reads it when
+    NumPy is imported, so it is overridden before that import, and
+    threadpoolctl raises a pool that was already created. Returns the thread
+    count the BLAS pool reports.
+    """
+    n = len(os.sched_getaffinity(0))
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = str(n)
+    try:
+        import threadpoolctl
+
+        threadpoolctl.threadpool_limits(n, user_api="blas")
+        pools = [p["num_threads"] for p in threadpoolctl.threadpool_info() if p.get("user_api") == "blas"]
+        return max(pools) if pools else n
+    except Exception:
+        return n
+
+
+def reference_kernels():
+    """The unmodified reference's own fused tied-CE functions on its CPU
+    (NumPy) backend, from the offline install in baseline/_ref, or None."""
+    ref = REPO / "baseline" / "_ref"
+    if not (ref / "NimbleML" / "__init__.py").exists():
+        return None
+    os.environ["NIMBLEML_DEVICE"] = "cpu"
+    os.environ["NIMBLEML_DTYPE"] = "float32"
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    from NimbleML.kernels import fused_tied_crossentropy_backward, fused_tied_crossentropy_forward
+
+    return fused_tied_crossentropy_forward, fused_tied_crossentropy_backward
+
+
 def cpu_reference_sample(cfg, seconds=12.0, max_rows=4096):
-    """Times the reference's CPU algorithm (oracle restatement, NumPy/BLAS fp32,
-    all host threads) on a row sample of the workload; returns a callable step
-    and the sample description."""
+    """A bounded CPU sample of the workload for the reference arm and the
+    cpu_baseline: the reference's own NimbleML.kernels.fused_tied_crossentropy_*
+    (NIMBLEML_DEVICE=cpu, fp32, BLAS on all host threads) when baseline/_ref
+    holds it, else the oracle's restatement of the same algorithm. Returns
+    (step callable, rows, sample description, kind, threads)."""
+    threads = all_host_threads()
     import numpy as np
 
-    from oracle import tied_ce_oracle as orc
-
+    ref = reference_kernels()
     rng = np.random.default_rng(1234)
     e = (rng.standard_normal((cfg["v"], cfg["d"]), dtype=np.float32) * np.float32(0.02))
 
@@ -149,29 +194,45 @@ def cpu_reference_sample(cfg, seconds=12.0, max_rows=4096):
         y = rng.integers(0, cfg["v"], rows, dtype=np.int64)
         return h, y
 
-    def run(h, y):
-        loss, hh, ww, logits, mx, se = orc.tied_forward(h, e, y, np.float32)
-        orc.tied_backward(1.0, hh, ww, y, logits, mx, se)
+    if ref is not None:
+        fwd, bwd = ref
+        kind = "reference"
+        what = ("the reference's own NimbleML.kernels.fused_tied_crossentropy_forward/_backward "
+                "(baseline/_ref, NIMBLEML_DEVICE=cpu)")
+
+        def run(h, y):
+            loss, hh, ww, logits, mx, se = fwd(h, e, y)
+            bwd(1.0, hh, ww, y, logits, mx, se)
+    else:
+        from oracle import tied_ce_oracle as orc
+
+        kind = "port"
+        what = ("the reference algorithm restated in oracle/tied_ce_oracle.py "
+                "(NimbleML/kernels/fused_*crossentropy.py)")
+
+        def run(h, y):
+            loss, hh, ww, logits, mx, se = orc.tied_forward(h, e, y, np.float32)
+            orc.tied_backward(1.0, hh, ww, y, logits, mx, se)
 
     rows = 32
     h, y = make(rows)
+    run(h, y)  # first call pays one-time costs (page faults, BLAS pool start)
     t0 = time.perf_counter()
     run(h, y)
     dt = time.perf_counter() - t0
     rows = int(min(max_rows, max(32, rows * seconds / max(dt, 1e-3))))
     rows = max(32, rows // 32 * 32)
     h, y = make(rows)
-    sample = (f"{rows} of {cfg['n']} token rows at full d={cfg['d']}, V={cfg['v']}; reference algorithm "
-              f"(oracle/tied_ce_oracle.py restating NimbleML/kernels/fused_*crossentropy.py) in NumPy "
-              f"fp32 with all BLAS threads (the reference's fp16 NumPy path has no BLAS)")
-    return (lambda: run(h, y)), rows, sample
+    sample = (f"{rows} of {cfg['n']} token rows at full d={cfg['d']}, V={cfg['v']}; {what} in NumPy fp32 with "
+              f"{threads} BLAS threads (the reference's fp16 NumPy matmul has no BLAS path)")
+    return (lambda: run(h, y)), rows, sample, kind, threads
 
 
 def run_reference_arm(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    step, rows, sample = cpu_reference_sample(cfg, seconds=6.0)
+    step, rows, sample, kind, threads = cpu_reference_sample(cfg, seconds=6.0)
     for _ in range(args.warmup):
         step()
     times = []
@@ -181,17 +242,80 @@ def run_reference_arm(args, cfg):
         times.append(time.perf_counter() - t0)
     t = statistics.mean(times)
     value = rows / t
-    cores = os.cpu_count()
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": cfg["workload"], "n_tokens": cfg["n"], "d_model": cfg["d"], "vocab": cfg["v"],
                    "sample_rows": rows, "parallelism": "host CPU"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss, dh, de, scale,
+                   n_rows=32, n_cls=8):
+    """Checks the last timed step's results on every rank against float64
+    recomputed on the device from the same inputs: sampled rows' lse and loss
+    terms (lse - target) at 2e-3, the loss as the mean of the per-row terms,
+    sampled rows of grad_hidden and sampled rows of this rank's grad_weights
+    shard at 1e-2 (relative 2-norm). Rank-local errors are maxed over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    dev = h.device
+    n = h.shape[0]
+    g = torch.Generator(device="cpu").manual_seed(5)
+    rows = torch.randperm(n, generator=g)[:n_rows].to(dev)
+    e64 = e_local.double()
+    s_loc = h[rows].double() @ e64.T                                     # (R, v_local)
+    if world > 1:
+        per = -(-v // world)
+        pad = torch.full((n_rows, per), float("-inf"), dtype=torch.float64, device=dev)
+        pad[:, : s_loc.shape[1]] = s_loc
+        allp = torch.empty((world, n_rows, per), dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(allp, pad, group=group)
+        s_full = allp.permute(1, 0, 2).reshape(n_rows, world * per)[:, :v]
+    else:
+        s_full = s_loc
+    y = labels[rows]
+    lse64 = torch.logsumexp(s_full, dim=1)
+    terms64 = lse64 - s_full.gather(1, y[:, None])[:, 0]
+    tgt = stats3[2].double().sum(0)                                      # (N,) target logit
+    terms = lse.double() - tgt
+    rel = lambda a, b: float((a - b).norm() / b.norm())
+    out = {"lse_rel": rel(lse.double()[rows], lse64), "loss_terms_rel": rel(terms[rows], terms64),
+           "loss_vs_mean_terms_rel": abs(float(loss) - float(terms.mean())) / float(terms.mean())}
+    # grad_hidden rows: sum over shards of G_rows . E_shard (float64).
+    gl = torch.exp(s_loc - lse64[:, None])
+    yl = y - v_off
+    own = (yl >= 0) & (yl < e_local.shape[0])
+    gl[own.nonzero()[:, 0], yl[own]] -= 1.0
+    dh_ref = (gl * (scale / n)) @ e64
+    if world > 1:
+        dist.all_reduce(dh_ref, group=group)
+    out["dh_rel"] = rel(dh.double()[rows], dh_ref)
+    # grad_weights rows of this rank's shard.
+    cls = torch.randperm(e_local.shape[0], generator=g)[:n_cls].to(dev)
+    h64 = h.double()
+    pc = torch.exp(h64 @ e64[cls].T - lse.double()[:, None])
+    pc -= (labels[:, None] == (cls[None, :] + v_off)).double()
+    de_ref = (pc * (scale / n)).T @ h64
+    out["de_rel"] = rel(de.double()[cls], de_ref)
+    del h64, pc
+    errs = torch.tensor([out[k] for k in ("lse_rel", "loss_terms_rel", "loss_vs_mean_terms_rel", "dh_rel",
+                                          "de_rel")], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(errs, op=dist.ReduceOp.MAX, group=group)
+    keys = ("lse_rel", "loss_terms_rel", "loss_vs_mean_terms_rel", "dh_rel", "de_rel")
+    out = {k: float(x) for k, x in zip(keys, errs.tolist())}
+    tol = {"lse_rel": 2e-3, "loss_terms_rel": 2e-3, "loss_vs_mean_terms_rel": 1e-5, "dh_rel": 1e-2,
+           "de_rel": 1e-2}
+    out["ok"] = all(out[k] <= tol[k] and math.isfinite(out[k]) for k in keys)
+    out["tolerances"] = tol
+    out["sample"] = f"{n_rows} token rows, {n_cls} vocab rows per rank, float64 on the device, max over ranks"
+    return out
 
 
 def run_c5(args):
@@ -332,11 +456,14 @@ def launches_per_step(cfg, world, slab_bytes):
     es = 4 if cfg["dtype"] == "float32" else 2
     cols = (slab_bytes or (2 << 30)) // (es * n)
     cols = max(256, cols // 256 * 256)
-    cols = min(cols, -(-((v_local + 1) // 2) // 256) * 256)
+    if world == 1:  # one GPU: at least two slabs (no buffer holds half the logits)
+        cols = min(cols, -(-((v_local + 1) // 2) // 256) * 256)
+    else:  # a shard of a split vocabulary: the byte budget alone
+        cols = min(cols, -(-v_local // 256) * 256)
     n_slabs = -(-v_local // cols)
     k = 2 + 1 + 3 * n_slabs  # fwd GEMM + row reduce, combine, 3 GEMMs per slab
     if cfg["dtype"] == "float32":
-        k += 4  # tf32 rounding copies in forward and backward
+        k += 2  # tf32 rounding of h and E, once per forward + backward
     return k, n_slabs
 
 
@@ -345,10 +472,14 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--warmup-seconds", type=float, default=4.0,
+                    help="keep warming up until this much time has passed, so every N is measured at "
+                         "steady-state power and clocks")
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS) + ["c5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -378,6 +509,7 @@ def main():
     n, d, v = cfg["n"], cfg["d"], cfg["v"]
     group = dist.group.WORLD if world > 1 else None
     v_off, v_local = vp.shard_range(v, rank, world)
+    scale = GRAD_SCALE[cfg["dtype"]]
 
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)  # identical h / labels on every rank
@@ -390,35 +522,60 @@ def main():
     gen_e.manual_seed(99 + rank)
     e_local = (torch.randn((v_local, d), generator=gen_e, device=dev) * 0.02).to(dtype).contiguous()
     ign = k._NO_IGNORE
-    ones = torch.ones(1, device=dev)
+    gscale = torch.full((1,), scale, device=dev)
 
-    fwd_ev = []
+    # Per-phase CUDA events of the timed steps (current stream unless noted).
+    phases = []
 
     def step(record=False):
+        ev = None
         if record:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-        part = k.shard_forward(h, e_local, labels, v_off)
+            names = ["start", "fwd_end", "combine_end", "compute_end", "comm_start", "comm_end", "end"]
+            ev = {nm: torch.cuda.Event(enable_timing=True) for nm in names}
+            ev["start"].record()
+        rounded = (k.round_tf32(h), k.round_tf32(e_local)) if dtype == torch.float32 else None
+        part = k.shard_forward(*(rounded or (h, e_local)), labels, v_off, rounded=rounded is not None)
         if record:
-            b.record()
-            fwd_ev.append((a, b))
+            ev["fwd_end"].record()
         stats3 = vp.gather_shard_stats(part, group)
         _, _, lse, loss, valid = k.combine(stats3, labels, v, ign)
-        st = k.TiedCEStats(lse=lse, valid_count=valid, ignore_index=ign, vocab_size=v, vocab_offset=v_off)
+        if record:
+            ev["combine_end"].record()
+        st = k.TiedCEStats(lse=lse, valid_count=valid, ignore_index=ign, vocab_size=v, vocab_offset=v_off,
+                           rounded=rounded)
         if world > 1:
-            vp.sharded_backward(ones, h, e_local, labels, st, group)
+            dh, de = vp.sharded_backward(gscale, h, e_local, labels, st, group, phase_events=ev)
         else:
-            k.shard_backward(ones, h, e_local, labels, st)
-        return loss
+            dh, de = k.shard_backward(gscale, h, e_local, labels, st)
+            if record:
+                ev["compute_end"].record()
+                ev["end"].record()
+        if record:
+            phases.append(ev)
+        return stats3, lse, loss, dh, de
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
+    # Warm-up: W steps, then more until --warmup-seconds have passed (the same
+    # count on every rank), so short multi-GPU runs are not timed before the
+    # GPUs reach their power-capped steady state.
+    t_w = time.perf_counter()
     for _ in range(args.warmup):
         step()
     barrier()
+    per_step = (time.perf_counter() - t_w) / args.warmup
+    extra = max(0, math.ceil((args.warmup_seconds - (time.perf_counter() - t_w)) / max(per_step, 1e-4)))
+    if world > 1:
+        t = torch.tensor([extra], device=dev, dtype=torch.int64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        extra = int(t[0])
+    for _ in range(extra):
+        step()
+    barrier()
+    warmup_steps = args.warmup + extra
     assert k.check_status(dev) == 0
     bus = None
     try:
@@ -436,18 +593,38 @@ def main():
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_start.record()
     for _ in range(args.steps):
-        step(record=True)
+        last = step(record=True)
     t_end.record()
     barrier()
     clocks = sampler.stop() if sampler else None
     elapsed = t_start.elapsed_time(t_end) / 1e3
-    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_ev)
     peak_extra = torch.cuda.max_memory_allocated(dev) - mem0
     assert k.check_status(dev) == 0
+
+    def mean_ms(a, b):
+        return statistics.mean(ev[a].elapsed_time(ev[b]) for ev in phases)
+
+    phase_ms = {"forward_gemm_and_row_reduce": mean_ms("start", "fwd_end"),
+                "stats_exchange_and_combine": mean_ms("fwd_end", "combine_end"),
+                "backward_gemms": mean_ms("combine_end", "compute_end"),
+                "exposed_grad_hidden_reduction": mean_ms("compute_end", "end")}
     if world > 1:
-        t = torch.tensor([elapsed, fwd_ms], device=dev, dtype=torch.float64)
+        phase_ms["grad_hidden_all_reduce"] = mean_ms("comm_start", "comm_end")
+        phase_ms["all_reduce_start_after_backward_start"] = mean_ms("combine_end", "comm_start")
+    fwd_ms = phase_ms["forward_gemm_and_row_reduce"]
+    if world > 1:
+        keys = sorted(phase_ms)
+        t = torch.tensor([elapsed] + [phase_ms[x] for x in keys], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed, fwd_ms = float(t[0]), float(t[1])
+        elapsed = float(t[0])
+        phase_ms = {x: float(val) for x, val in zip(keys, t[1:].tolist())}
+        fwd_ms = phase_ms["forward_gemm_and_row_reduce"]
+
+    parity = None
+    if not args.no_parity:
+        stats3, lse, loss, dh, de = last
+        parity = sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss, dh, de, scale)
+    del last
 
     # ---- end to end through the public API: host inputs, H2D copy, loss D2H.
     e2e = None
@@ -489,7 +666,7 @@ def main():
                 hd = head.hidden_from_host(h_host).requires_grad_(True)
                 yd = y_host.to(dev, non_blocking=True)
                 loss = head.loss(hd, yd)
-            loss.backward()
+            (loss * scale).backward()  # the same loss scale as the device-timed step
             return float(loss)
 
         for i in range(args.warmup):
@@ -511,6 +688,8 @@ def main():
     if rank != 0:
         dist.barrier() if world > 1 else None
         dist.destroy_process_group() if world > 1 else None
+        if parity is not None and not parity["ok"]:
+            sys.exit(3)
         return
 
     burst, sustained, hbm, peak_kind = _peaks()
@@ -524,19 +703,24 @@ def main():
     traffic = _profile_traffic(args.config) if world == 1 else None
     line = {
         "metric": METRIC, "value": n / step_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
+        "warmup": warmup_steps, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": DTYPE_TAG[cfg["dtype"]], "data": "synthetic",
         "config": {"workload": cfg["workload"], "n_tokens": n, "batch": cfg["batch"], "seq_len": cfg["seq"],
                    "d_model": d, "vocab": v, "parallelism": f"vocab-sharded x{world}" if world > 1 else "1 GPU",
                    "l2": "inputs larger than L2 (h %.0f MB, E %.0f MB), no flush" % (
                        n * d * h.element_size() / 1e6, v * d * h.element_size() / 1e6),
-                   "backward_slabs": n_slabs},
-        "roofline": {"bound": "tensor", "kernel": "tc_gemm_tn_kernel<EPI_CE_FWD>, wide 256x256 tiles (+ row reduce)",
+                   "grad_scale": scale,
+                   "grad_dtypes": {"grad_hidden": "f32 (all-reduced)" if world > 1 else DTYPE_TAG[cfg["dtype"]],
+                                   "grad_weights": DTYPE_TAG[cfg["dtype"]]},
+                   "backward_slabs": n_slabs, "warmup_seconds": args.warmup_seconds},
+        "roofline": {"bound": "tensor", "kernel": "tc_gemm_tn_kernel<EPI_CE_FWD> (+ ce_row_reduce_kernel)",
                      "achieved": fwd_tflops, "peak": sustained, "unit": "TFLOP/s",
                      "frac": fwd_tflops / sustained, "peak_kind": f"{peak_kind} sustained bf16 cuBLAS",
                      "traffic": traffic, "flops_per_launch": flops_fwd_launch,
                      "step_tflops_per_gpu": step_tflops, "step_frac_of_measured": step_tflops / sustained,
                      "step_frac_of_datasheet_dense": step_tflops / datasheet},
+        "phases_ms": phase_ms,
+        "parity": parity,
         "gpu_launches": k_launch * args.steps,
         "clocks": clocks,
         "memory": {"peak_extra_bytes": int(peak_extra), "materialised_logits_bytes": n * v * h.element_size(),
@@ -544,17 +728,20 @@ def main():
         "e2e": e2e,
     }
     if world == 1 and not args.no_cpu_baseline:
-        step_fn, rows, sample = cpu_reference_sample(cfg)
+        step_fn, rows, sample, kind, threads = cpu_reference_sample(cfg)
         step_fn()
         t0 = time.perf_counter()
         step_fn()
         tc = time.perf_counter() - t0
-        line["cpu_baseline"] = {"value": rows / tc, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+        line["cpu_baseline"] = {"value": rows / tc, "unit": "tokens/s", "cores": threads, "kind": kind,
                                 "sample": sample}
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if parity is not None and not parity["ok"]:
+        print("parity check FAILED: " + json.dumps(parity), file=sys.stderr, flush=True)
+        sys.exit(3)
 
 
 if __name__ == "__main__":

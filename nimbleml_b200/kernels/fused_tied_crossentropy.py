@@ -101,6 +101,7 @@ def check_status(device: torch.device, *, clear: bool = True) -> int:
     val = int(buf.item())
     if clear and val:
         buf.zero_()
+        _monitor(device).pending = False  # an older asynchronous copy would repeat this value
     _raise_for(val)
     return val
 

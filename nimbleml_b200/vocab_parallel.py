@@ -80,13 +80,19 @@ def _comm_stream(device: torch.device) -> torch.cuda.Stream:
     return st
 
 
-def sharded_backward(grad_scale, h, w, labels, stats, group=None, *, grad_weights=None, accumulate=False):
+def sharded_backward(grad_scale, h, w, labels, stats, group=None, *, grad_weights=None, accumulate=False,
+                     phase_events=None):
     """Backward of one vocab shard with the grad_hidden all_reduce overlapped.
 
     The library computes the last slab's grad_hidden first and records an
     event; the fp32 all_reduce then runs on a side stream while the last
     grad_weights GEMM runs on all but COMM_SMS SMs. Returns (grad_hidden
     summed over ranks, fp32; grad_weights of this shard).
+
+    ``phase_events``: optional dict of four timing-enabled CUDA events,
+    recorded at the end of the backward kernels ("compute_end", current
+    stream), around the all_reduce ("comm_start", "comm_end", side stream)
+    and once the current stream has caught up with it ("end").
     """
     from nimbleml_b200.kernels.fused_tied_crossentropy import shard_backward
 
@@ -99,12 +105,20 @@ def sharded_backward(grad_scale, h, w, labels, stats, group=None, *, grad_weight
     grad_h, grad_w = shard_backward(grad_scale, h, w, labels, stats, grad_hidden_dtype=torch.float32,
                                     grad_weights=grad_weights, accumulate=accumulate, ready_event=ready,
                                     last_de_max_ctas=max(1, sms - COMM_SMS))
+    if phase_events:
+        phase_events["compute_end"].record()
     comm = _comm_stream(dev)
     comm.wait_event(ready)
     with torch.cuda.stream(comm):
+        if phase_events:
+            phase_events["comm_start"].record()
         dist.all_reduce(grad_h, op=dist.ReduceOp.SUM, group=group)
+        if phase_events:
+            phase_events["comm_end"].record()
     grad_h.record_stream(comm)
     torch.cuda.current_stream(dev).wait_stream(comm)
+    if phase_events:
+        phase_events["end"].record()
     return grad_h, grad_w
 
 

@@ -58,3 +58,50 @@ def test_available_is_false_without_gpu():
 
     if not torch.cuda.is_available():
         assert native.available() is False
+
+
+def test_pybind_module_exports_device_entry_points():
+    """The pybind11 module (the reference extension's binding pattern) loads without a GPU."""
+    import sys
+
+    from nimbleml_b200._native_loader import DTYPE_F16, native
+    from nimbleml_b200.build_native import LIB_DIR
+
+    sys.path.insert(0, str(LIB_DIR))
+    import nimbleml_tied_ce_native as m
+
+    for name in ("tied_ce_available", "tied_ce_forward_device", "tied_ce_combine_device", "tied_ce_backward_device",
+                 "tied_ce_forward_workspace_size", "tied_ce_backward_workspace_size"):
+        assert callable(getattr(m, name)), name
+    assert m.tied_ce_forward_workspace_size(4096, 1024, 50257, DTYPE_F16) == \
+        native.forward_workspace_size(4096, 1024, 50257, DTYPE_F16)
+    with pytest.raises(RuntimeError, match="sizes must be positive"):
+        m.tied_ce_forward_workspace_size(8, 0, 10, DTYPE_F16)
+
+
+def test_reference_binding_rebinds_the_reference_names():
+    """install() swaps the fused tied-CE functions everywhere the reference looks them up."""
+    import os
+    import subprocess
+    import sys
+
+    ref = REPO / "baseline" / "_ref"
+    if not (ref / "NimbleML" / "__init__.py").exists():
+        pytest.skip("baseline/_ref holds no reference install")
+    code = f"""
+import sys
+sys.path[:0] = [{str(ref)!r}, {str(REPO)!r}]
+import NimbleML.kernels as K, NimbleML.kernels.fused_tied_crossentropy as F, NimbleML.losses.cross_entropy as C
+from nimbleml_b200.integration import reference_binding as rb
+orig = C.fused_tied_crossentropy_forward
+prev = rb.install()
+for mod in (K, F, C):
+    assert mod.fused_tied_crossentropy_forward is rb.fused_tied_crossentropy_forward
+    assert mod.fused_tied_crossentropy_backward is rb.fused_tied_crossentropy_backward
+rb.uninstall(prev)
+assert C.fused_tied_crossentropy_forward is orig
+print("ok")
+"""
+    r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, NIMBLEML_DEVICE="cpu"),
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stderr[-2000:]
