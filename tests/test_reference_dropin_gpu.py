@@ -92,8 +92,13 @@ def test_reference_compute_loss_on_b200_kernels(ignore, tmp_path):
     assert int(ours["n"]) == int(ref["n"]) > 0
     loss_ref, loss = float(ref["loss"]), float(ours["loss"])
     assert abs(loss - loss_ref) <= 1e-5 * abs(loss_ref), (loss, loss_ref)
+    # A grad that is zero in exact arithmetic (the attention key bias: softmax
+    # ignores a shift shared by a query's scores) holds only rounding noise
+    # (~1e-9) in both runs, so each grad's error is relative to its own norm
+    # or, if larger, to 1e-6 of the norm of all grads.
+    total = np.sqrt(sum(float(np.sum(ref[f"g{i}"] ** 2)) for i in range(int(ref["n"]))))
     for i in range(int(ref["n"])):
         g_ref, g = ref[f"g{i}"], ours[f"g{i}"]
         assert g.shape == g_ref.shape
-        err = np.linalg.norm(g - g_ref) / max(np.linalg.norm(g_ref), 1e-30)
-        assert err <= 1e-3, (i, err)
+        err = np.linalg.norm(g - g_ref) / max(np.linalg.norm(g_ref), 1e-6 * total)
+        assert err <= 1e-3, (i, err, float(np.linalg.norm(g_ref)))

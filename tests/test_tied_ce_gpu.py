@@ -356,13 +356,25 @@ def test_overlap_entry_point_matches_backward():
     hd, ed, yd = to_dev(h, torch.float16), to_dev(e, torch.float16), torch.as_tensor(y).cuda()
     loss, hh, ww, st, mx, se = k.fused_tied_crossentropy_forward(hd, ed, yd)
     one = torch.ones(1, device="cuda")
-    a = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32)
+    # Same slabs in both (a 1024-column budget): bit-identical results.
+    slab = 640 * 2 * 1024
+    a = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32, slab_bytes=slab)
     ev = torch.cuda.Event()
     ev.record()
-    b = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32, ready_event=ev, last_de_max_ctas=20)
+    b = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32, ready_event=ev, last_de_max_ctas=20,
+                         slab_bytes=slab)
     torch.cuda.synchronize()
     assert ev.query()
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    # Default budget: the overlap entry point (a shard of a split vocabulary)
+    # takes the shard in one slab, the plain backward in two; both match float64.
+    c = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32, ready_event=ev, last_de_max_ctas=20)
+    torch.cuda.synchronize()
+    l64, dh64, de64, _, _ = orc.row_chunked_reference(rounded64(h, torch.float16), rounded64(e, torch.float16), y)
+    for dh, de in (a, c):
+        assert rel(dh.double().cpu().numpy(), dh64) < 1e-2
+        assert rel(de.double().cpu().numpy(), de64) < 1e-2
+    assert torch.equal(a[1], c[1])  # dE rows: the same K loop over the tokens whatever the slab
 
 
 def test_empty_batch():
