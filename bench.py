@@ -710,8 +710,10 @@ def main():
                    "l2": "inputs larger than L2 (h %.0f MB, E %.0f MB), no flush" % (
                        n * d * h.element_size() / 1e6, v * d * h.element_size() / 1e6),
                    "grad_scale": scale,
-                   "grad_dtypes": {"grad_hidden": "f32 (all-reduced)" if world > 1 else DTYPE_TAG[cfg["dtype"]],
+                   "grad_dtypes": {"grad_hidden": (DTYPE_TAG[str(vp.DH_REDUCE_DTYPE).replace("torch.", "")]
+                                                   + " (all-reduced)") if world > 1 else DTYPE_TAG[cfg["dtype"]],
                                    "grad_weights": DTYPE_TAG[cfg["dtype"]]},
+                   "last_de_capped_fraction": vp.CAPPED_FRACTION if world > 1 else None,
                    "backward_slabs": n_slabs, "warmup_seconds": args.warmup_seconds},
         "roofline": {"bound": "tensor", "kernel": "tc_gemm_tn_kernel<EPI_CE_FWD> (+ ce_row_reduce_kernel)",
                      "achieved": fwd_tflops, "peak": sustained, "unit": "TFLOP/s",

@@ -76,9 +76,13 @@ enum {
  * multi-GPU path). Same arguments and results, plus: the last slab computes
  * grad_hidden before its grad_weights rows and records
  * grad_hidden_ready_event (a cudaEvent_t) on `stream` right after it; the
- * last grad_weights GEMM then runs on at most last_de_max_ctas SMs (0 = all),
- * leaving SMs for a collective the caller enqueues on another stream after
- * waiting on the event. */
+ * first capped_fraction of that slab's grad_weights rows (rounded up to
+ * 256-row tiles; >= 1: all of them) then run on at most last_de_max_ctas SMs
+ * (0 = all), leaving SMs for a collective the caller enqueues on another
+ * stream after waiting on the event, and the remaining rows run on all SMs.
+ * Slabs follow the slab_bytes budget alone (the shard is at most half of a
+ * split vocabulary): size the workspace with
+ * nimble_tied_ce_backward_overlap_workspace_size. */
 NIMBLE_API int nimble_tied_ce_backward_overlap(const float* grad_scale, const void* hidden,
                                                const void* weights, const int64_t* labels,
                                                const float* lse, const float* valid_count,
@@ -89,7 +93,7 @@ NIMBLE_API int nimble_tied_ce_backward_overlap(const float* grad_scale, const vo
                                                int accumulate_grad_weights, size_t slab_bytes,
                                                void* workspace, size_t workspace_bytes, int* status,
                                                void* stream, void* grad_hidden_ready_event,
-                                               int last_de_max_ctas);
+                                               int last_de_max_ctas, float capped_fraction);
 
 /* 1 when a compute-capability 10.x device is visible, else 0. Mirrors the
  * reference's availability flags (native/src/module.cpp:13-17,221-227). */

@@ -101,7 +101,7 @@ SIGNATURES = {
         _c_int,
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
          _c_int, _c_vp, _c_int, _c_vp, _c_int, _c_int, _c_size, _c_vp, _c_size, _c_vp,
-         _c_vp, _c_vp, _c_int]),
+         _c_vp, _c_vp, _c_int, ctypes.c_float]),
 }
 
 

@@ -1088,7 +1088,7 @@ int backward_impl(const float* grad_scale, const void* hidden, const void* weigh
                   int64_t v_offset, int64_t ignore_index, int dtype, void* grad_hidden, int grad_hidden_dtype,
                   void* grad_weights, int grad_weights_dtype, int accumulate_grad_weights, size_t slab_bytes,
                   void* workspace, size_t workspace_bytes, int* status, void* stream, void* dh_done_event,
-                  int last_de_max_ctas) {
+                  int last_de_max_ctas, float capped_fraction) {
   if (int rc = check_common(hidden, weights, labels, n_tokens, d_model, v_local, dtype, true, true)) return rc;
   if (!grad_weights || !grad_scale || !valid_count || (n_tokens > 0 && (!grad_hidden || !lse)))
     return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
@@ -1144,9 +1144,11 @@ int backward_impl(const float* grad_scale, const void* hidden, const void* weigh
     const bool last = sl == L.n_slabs - 1;
     // 2) dE[c0:c0+vc] = G^T h: A = G read MN-major ([tokens x vc]), B = h
     //    read MN-major ([tokens x d]); K = tokens.
-    auto run_de = [&](int max_ctas) -> int {
+    // dE rows [r0, r1) of the slab on at most max_ctas SMs (0 = all).
+    auto run_de = [&](int max_ctas, int64_t r0, int64_t r1) -> int {
+      if (r1 <= r0) return NIMBLE_OK;
       EpiParams ee{};
-      ee.out = static_cast<uint8_t*>(grad_weights) + elem_size(grad_weights_dtype) * c0 * d_model;
+      ee.out = static_cast<uint8_t*>(grad_weights) + elem_size(grad_weights_dtype) * (c0 + r0) * d_model;
       ee.ld_out = d_model;
       ee.out_dtype = grad_weights_dtype;
       ee.alpha_num = grad_scale;
@@ -1154,8 +1156,8 @@ int backward_impl(const float* grad_scale, const void* hidden, const void* weigh
       ee.alpha_mult = 1.0f / gscale;
       ee.accum_out = accumulate_grad_weights ? 1 : 0;
       ee.status = status;
-      return gemm_dispatch<EPI_STORE, true, true>(dtype, g, L.slab, h, d_model, vc, d_model, n_tokens, ee, s,
-                                                  max_ctas);
+      return gemm_dispatch<EPI_STORE, true, true>(dtype, static_cast<uint8_t*>(g) + es * r0, L.slab, h, d_model,
+                                                  r1 - r0, d_model, n_tokens, ee, s, max_ctas);
     };
     // 3) dh (+)= G E[c0:c0+vc]: A = G K-major, B = E slab read MN-major
     //    ([vc x d]); K = slab columns.
@@ -1182,11 +1184,17 @@ int backward_impl(const float* grad_scale, const void* hidden, const void* weigh
       // grad_hidden is final after this slab's dh GEMM: announce it, then
       // run the last dE GEMM (optionally on fewer SMs) while the caller
       // reduces grad_hidden across ranks.
+      // Its first rows run beside the caller's reduction on fewer SMs, the
+      // rest on all SMs once the reduction is expected to be done.
       if (int rc = run_dh()) return rc;
       NIMBLE_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(dh_done_event), s));
-      if (int rc = run_de(last_de_max_ctas)) return rc;
+      int64_t split = vc;
+      if (capped_fraction < 1.0f)
+        split = std::min<int64_t>(vc, round_up(static_cast<int64_t>(capped_fraction * static_cast<double>(vc)), kBN));
+      if (int rc = run_de(last_de_max_ctas, 0, split)) return rc;
+      if (int rc = run_de(0, split, vc)) return rc;
     } else {
-      if (int rc = run_de(0)) return rc;
+      if (int rc = run_de(0, 0, vc)) return rc;
       if (int rc = run_dh()) return rc;
     }
   }
@@ -1203,7 +1211,8 @@ extern "C" int nimble_tied_ce_backward(const float* grad_scale, const void* hidd
                                        void* stream) {
   return backward_impl(grad_scale, hidden, weights, labels, lse, valid_count, n_tokens, d_model, v_local, v_offset,
                        ignore_index, dtype, grad_hidden, grad_hidden_dtype, grad_weights, grad_weights_dtype,
-                       accumulate_grad_weights, slab_bytes, workspace, workspace_bytes, status, stream, nullptr, 0);
+                       accumulate_grad_weights, slab_bytes, workspace, workspace_bytes, status, stream, nullptr, 0,
+                       1.0f);
 }
 
 extern "C" int nimble_tied_ce_backward_overlap(const float* grad_scale, const void* hidden, const void* weights,
@@ -1213,13 +1222,15 @@ extern "C" int nimble_tied_ce_backward_overlap(const float* grad_scale, const vo
                                                int grad_hidden_dtype, void* grad_weights, int grad_weights_dtype,
                                                int accumulate_grad_weights, size_t slab_bytes, void* workspace,
                                                size_t workspace_bytes, int* status, void* stream,
-                                               void* grad_hidden_ready_event, int last_de_max_ctas) {
+                                               void* grad_hidden_ready_event, int last_de_max_ctas,
+                                               float capped_fraction) {
   if (!grad_hidden_ready_event) return fail(NIMBLE_ERR_INVALID_ARG, "null grad_hidden_ready_event");
   if (last_de_max_ctas < 0) return fail(NIMBLE_ERR_INVALID_ARG, "last_de_max_ctas must be >= 0");
+  if (!(capped_fraction >= 0.0f)) return fail(NIMBLE_ERR_INVALID_ARG, "capped_fraction must be >= 0");
   return backward_impl(grad_scale, hidden, weights, labels, lse, valid_count, n_tokens, d_model, v_local, v_offset,
                        ignore_index, dtype, grad_hidden, grad_hidden_dtype, grad_weights, grad_weights_dtype,
                        accumulate_grad_weights, slab_bytes, workspace, workspace_bytes, status, stream,
-                       grad_hidden_ready_event, last_de_max_ctas);
+                       grad_hidden_ready_event, last_de_max_ctas, capped_fraction);
 }
 
 // ================================================================ diagnostics

@@ -247,14 +247,16 @@ def combine(shard_stats: torch.Tensor, labels: torch.Tensor, vocab_size: int, ig
 def shard_backward(grad_scale: torch.Tensor, h: torch.Tensor, w: torch.Tensor, labels: torch.Tensor,
                    stats: TiedCEStats, *, grad_hidden_dtype=None, grad_weights: Optional[torch.Tensor] = None,
                    accumulate: bool = False, slab_bytes: Optional[int] = None,
-                   ready_event: Optional[torch.cuda.Event] = None, last_de_max_ctas: int = 0):
+                   ready_event: Optional[torch.cuda.Event] = None, last_de_max_ctas: int = 0,
+                   capped_fraction: float = 1.0):
     """(grad_hidden partial over this shard, grad_weights of the shard).
 
     ``slab_bytes`` bounds the vocab slab's G scratch (default: the
     NIMBLEML_TIED_CE_SLAB_BYTES environment value, else the library's 2 GiB).
     With ``ready_event`` the event is recorded as soon as grad_hidden is final
-    and the last grad_weights GEMM runs on at most ``last_de_max_ctas`` SMs,
-    so a collective on grad_hidden can overlap it.
+    and the first ``capped_fraction`` of the last slab's grad_weights rows run
+    on at most ``last_de_max_ctas`` SMs (the rest on all SMs), so a
+    collective on grad_hidden can overlap them.
     """
     n, d = h.shape
     v_local = w.shape[0]
@@ -280,7 +282,8 @@ def shard_backward(grad_scale: torch.Tensor, h: torch.Tensor, w: torch.Tensor, l
     if ready_event is None:
         native.call("nimble_tied_ce_backward", *args)
     else:
-        native.call("nimble_tied_ce_backward_overlap", *args, ready_event.cuda_event, int(last_de_max_ctas))
+        native.call("nimble_tied_ce_backward_overlap", *args, ready_event.cuda_event, int(last_de_max_ctas),
+                    float(capped_fraction))
     snapshot_status(dev)
     return grad_h, grad_weights
 

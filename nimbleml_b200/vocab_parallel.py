@@ -28,6 +28,15 @@ import torch.distributed as dist
 # GEMM runs (NIMBLEML_TIED_CE_COMM_SMS, default 32; with 8 at 8 ranks NCCL is
 # starved and the reduction waits for the GEMM).
 COMM_SMS = int(os.environ.get("NIMBLEML_TIED_CE_COMM_SMS", "32"))
+# Share of the last grad_weights GEMM's rows that run beside the reduction on
+# the capped SM count; the rest run on all SMs (NIMBLEML_TIED_CE_CAPPED_FRACTION,
+# 1 = the whole GEMM capped).
+CAPPED_FRACTION = float(os.environ.get("NIMBLEML_TIED_CE_CAPPED_FRACTION", "1.0"))
+# Element type of the grad_hidden partials and of their all_reduce
+# (NIMBLEML_TIED_CE_DH_REDUCE_DTYPE: float32, float16 or bfloat16). 16-bit
+# halves the bytes on NVLink; partial sums then round to 16 bits, so use it
+# with a loss scale that keeps fp16 grads in their normal range.
+DH_REDUCE_DTYPE = getattr(torch, os.environ.get("NIMBLEML_TIED_CE_DH_REDUCE_DTYPE", "float32"))
 _comm_streams: dict = {}
 
 
@@ -86,8 +95,10 @@ def sharded_backward(grad_scale, h, w, labels, stats, group=None, *, grad_weight
 
     The library computes the last slab's grad_hidden first and records an
     event; the fp32 all_reduce then runs on a side stream while the last
-    grad_weights GEMM runs on all but COMM_SMS SMs. Returns (grad_hidden
-    summed over ranks, fp32; grad_weights of this shard).
+    grad_weights GEMM runs on all but COMM_SMS SMs (its first
+    CAPPED_FRACTION of rows; the rest on all SMs). Returns (grad_hidden
+    summed over ranks, in DH_REDUCE_DTYPE, fp32 by default; grad_weights of
+    this shard).
 
     ``phase_events``: optional dict of four timing-enabled CUDA events,
     recorded at the end of the backward kernels ("compute_end", current
@@ -102,9 +113,9 @@ def sharded_backward(grad_scale, h, w, labels, stats, group=None, *, grad_weight
     ready = torch.cuda.Event()
     ready.record()  # creates the event; re-recorded by the library
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    grad_h, grad_w = shard_backward(grad_scale, h, w, labels, stats, grad_hidden_dtype=torch.float32,
+    grad_h, grad_w = shard_backward(grad_scale, h, w, labels, stats, grad_hidden_dtype=DH_REDUCE_DTYPE,
                                     grad_weights=grad_weights, accumulate=accumulate, ready_event=ready,
-                                    last_de_max_ctas=max(1, sms - COMM_SMS))
+                                    last_de_max_ctas=max(1, sms - COMM_SMS), capped_fraction=CAPPED_FRACTION)
     if phase_events:
         phase_events["compute_end"].record()
     comm = _comm_stream(dev)

@@ -363,9 +363,13 @@ def test_overlap_entry_point_matches_backward():
     ev.record()
     b = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32, ready_event=ev, last_de_max_ctas=20,
                          slab_bytes=slab)
+    # The last dE GEMM split into a capped part and an uncapped part.
+    b2 = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32, ready_event=ev, last_de_max_ctas=20,
+                          slab_bytes=slab, capped_fraction=0.4)
     torch.cuda.synchronize()
     assert ev.query()
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    assert torch.equal(a[0], b2[0]) and torch.equal(a[1], b2[1])
     # Default budget: the overlap entry point (a shard of a split vocabulary)
     # takes the shard in one slab, the plain backward in two; both match float64.
     c = k.shard_backward(one, hh, ww, yd, st, grad_hidden_dtype=torch.float32, ready_event=ev, last_de_max_ctas=20)
