@@ -480,6 +480,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="profiling aid: one process computes rank 0's vocab shard of this many ranks through "
+                         "the sharded backward entry point, with no collectives (not a bench line)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -508,7 +511,8 @@ def main():
     dtype = getattr(torch, cfg["dtype"])
     n, d, v = cfg["n"], cfg["d"], cfg["v"]
     group = dist.group.WORLD if world > 1 else None
-    v_off, v_local = vp.shard_range(v, rank, world)
+    emulate = args.shard_of if world == 1 and args.shard_of > 1 else 1
+    v_off, v_local = vp.shard_range(v, rank, world * emulate)
     scale = GRAD_SCALE[cfg["dtype"]]
 
     gen = torch.Generator(device=dev)
@@ -545,6 +549,15 @@ def main():
                            rounded=rounded)
         if world > 1:
             dh, de = vp.sharded_backward(gscale, h, e_local, labels, st, group, phase_events=ev)
+        elif emulate > 1:
+            ready = torch.cuda.Event()
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            dh, de = k.shard_backward(gscale, h, e_local, labels, st, grad_hidden_dtype=vp.dh_reduce_dtype(dtype),
+                                      ready_event=ready, last_de_max_ctas=max(1, sms - vp.COMM_SMS),
+                                      capped_fraction=vp.CAPPED_FRACTION)
+            if record:
+                ev["compute_end"].record()
+                ev["end"].record()
         else:
             dh, de = k.shard_backward(gscale, h, e_local, labels, st)
             if record:
@@ -621,7 +634,7 @@ def main():
         fwd_ms = phase_ms["forward_gemm_and_row_reduce"]
 
     parity = None
-    if not args.no_parity:
+    if not args.no_parity and emulate == 1:
         stats3, lse, loss, dh, de = last
         parity = sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss, dh, de, scale)
     del last
@@ -702,7 +715,8 @@ def main():
     k_launch, n_slabs = launches_per_step(cfg, world, k.SLAB_BYTES)
     traffic = _profile_traffic(args.config) if world == 1 else None
     line = {
-        "metric": METRIC, "value": n / step_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC if emulate == 1 else f"profiling: rank-0 shard of {emulate} on one GPU, no collectives",
+        "value": n / step_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": warmup_steps, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": DTYPE_TAG[cfg["dtype"]], "data": "synthetic",
         "config": {"workload": cfg["workload"], "n_tokens": n, "batch": cfg["batch"], "seq_len": cfg["seq"],
@@ -710,7 +724,7 @@ def main():
                    "l2": "inputs larger than L2 (h %.0f MB, E %.0f MB), no flush" % (
                        n * d * h.element_size() / 1e6, v * d * h.element_size() / 1e6),
                    "grad_scale": scale,
-                   "grad_dtypes": {"grad_hidden": (DTYPE_TAG[str(vp.DH_REDUCE_DTYPE).replace("torch.", "")]
+                   "grad_dtypes": {"grad_hidden": (DTYPE_TAG[str(vp.dh_reduce_dtype(dtype)).replace("torch.", "")]
                                                    + " (all-reduced)") if world > 1 else DTYPE_TAG[cfg["dtype"]],
                                    "grad_weights": DTYPE_TAG[cfg["dtype"]]},
                    "last_de_capped_fraction": vp.CAPPED_FRACTION if world > 1 else None,

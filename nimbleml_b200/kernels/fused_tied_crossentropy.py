@@ -282,6 +282,8 @@ def shard_backward(grad_scale: torch.Tensor, h: torch.Tensor, w: torch.Tensor, l
     if ready_event is None:
         native.call("nimble_tied_ce_backward", *args)
     else:
+        if ready_event.cuda_event == 0:
+            ready_event.record()  # torch creates the CUDA event at its first record; the library re-records it
         native.call("nimble_tied_ce_backward_overlap", *args, ready_event.cuda_event, int(last_de_max_ctas),
                     float(capped_fraction))
     snapshot_status(dev)

@@ -33,10 +33,17 @@ COMM_SMS = int(os.environ.get("NIMBLEML_TIED_CE_COMM_SMS", "32"))
 # 1 = the whole GEMM capped).
 CAPPED_FRACTION = float(os.environ.get("NIMBLEML_TIED_CE_CAPPED_FRACTION", "1.0"))
 # Element type of the grad_hidden partials and of their all_reduce
-# (NIMBLEML_TIED_CE_DH_REDUCE_DTYPE: float32, float16 or bfloat16). 16-bit
-# halves the bytes on NVLink; partial sums then round to 16 bits, so use it
-# with a loss scale that keeps fp16 grads in their normal range.
-DH_REDUCE_DTYPE = getattr(torch, os.environ.get("NIMBLEML_TIED_CE_DH_REDUCE_DTYPE", "float32"))
+# (NIMBLEML_TIED_CE_DH_REDUCE_DTYPE: auto, float32, float16 or bfloat16).
+# "auto" reduces bfloat16 partials for 16-bit inputs (half the NVLink bytes of
+# fp32, fp32's exponent range so no loss scale is needed; ~3e-3 relative
+# error against the 1e-2 grad tolerance) and float32 partials for fp32 inputs.
+_DH_REDUCE = os.environ.get("NIMBLEML_TIED_CE_DH_REDUCE_DTYPE", "auto")
+
+
+def dh_reduce_dtype(compute_dtype: torch.dtype) -> torch.dtype:
+    if _DH_REDUCE != "auto":
+        return getattr(torch, _DH_REDUCE)
+    return torch.float32 if compute_dtype == torch.float32 else torch.bfloat16
 _comm_streams: dict = {}
 
 
@@ -97,8 +104,8 @@ def sharded_backward(grad_scale, h, w, labels, stats, group=None, *, grad_weight
     event; the fp32 all_reduce then runs on a side stream while the last
     grad_weights GEMM runs on all but COMM_SMS SMs (its first
     CAPPED_FRACTION of rows; the rest on all SMs). Returns (grad_hidden
-    summed over ranks, in DH_REDUCE_DTYPE, fp32 by default; grad_weights of
-    this shard).
+    summed over ranks, in dh_reduce_dtype(h.dtype); grad_weights of this
+    shard).
 
     ``phase_events``: optional dict of four timing-enabled CUDA events,
     recorded at the end of the backward kernels ("compute_end", current
@@ -111,9 +118,8 @@ def sharded_backward(grad_scale, h, w, labels, stats, group=None, *, grad_weight
         return shard_backward(grad_scale, h, w, labels, stats, grad_weights=grad_weights, accumulate=accumulate)
     dev = h.device
     ready = torch.cuda.Event()
-    ready.record()  # creates the event; re-recorded by the library
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    grad_h, grad_w = shard_backward(grad_scale, h, w, labels, stats, grad_hidden_dtype=DH_REDUCE_DTYPE,
+    grad_h, grad_w = shard_backward(grad_scale, h, w, labels, stats, grad_hidden_dtype=dh_reduce_dtype(h.dtype),
                                     grad_weights=grad_weights, accumulate=accumulate, ready_event=ready,
                                     last_de_max_ctas=max(1, sms - COMM_SMS), capped_fraction=CAPPED_FRACTION)
     if phase_events:
