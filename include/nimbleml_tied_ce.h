@@ -281,21 +281,33 @@ NIMBLE_API int nimble_rmsnorm_backward_workspace_size(int64_t n_rows, int64_t d_
 
 /* RMSNorm backward (NimbleML/kernels/fused_rmsnorm.py:161-217): grad_x in the
  * compute dtype and grad_gamma in fp32 (added to grad_gamma when
- * accumulate_grad_gamma != 0). */
+ * accumulate_grad_gamma != 0). grad_dtype is the compute dtype or
+ * NIMBLE_DTYPE_F32: the final norm before the tied head reads the head's
+ * fp32 grad_hidden directly, with no 16-bit copy in between. */
 NIMBLE_API int nimble_rmsnorm_backward(const void* grad, const void* x, const void* gamma, const float* ms,
                                        const float* rms, int64_t n_rows, int64_t d_model, float eps,
-                                       int dtype, void* grad_x, float* grad_gamma,
+                                       int dtype, int grad_dtype, void* grad_x, float* grad_gamma,
                                        int accumulate_grad_gamma, void* workspace,
                                        size_t workspace_bytes, void* stream);
 
-/* grad_weights[ids[i], :] += grad_out[i, :] into an fp32 (vocab x d) grad —
- * the input-embedding share of the tied matrix's grad
- * (NimbleML/kernels/embedding_scatter.py:39-81). Uses fp32 atomics, so the
- * summation order of repeated ids is not fixed. Out-of-range ids are skipped
- * and set NIMBLE_STATUS_BAD_LABEL. */
+/* Bytes of workspace nimble_embedding_scatter_add needs for n_rows ids and
+ * a shard of vocab_rows rows (keys and row indices of a device radix sort
+ * and its temporary storage). Queries the CUDA device. */
+NIMBLE_API int nimble_embedding_scatter_add_workspace_size(int64_t n_rows, int64_t vocab_rows, size_t* bytes);
+
+/* grad_weights[ids[i] - vocab_offset, :] += grad_out[i, :] into the fp32
+ * (vocab_rows x d) grad of the tied matrix's rows [vocab_offset,
+ * vocab_offset + vocab_rows) — the input embedding's share of the tied grad
+ * (NimbleML/kernels/embedding_scatter.py:39-81, NimbleML/layers/embedding.py:138-148).
+ * Deterministic: the rows of each id are added in ascending row order onto
+ * the existing grad row, the loop order of the reference's CPU scatter
+ * (native/src/scatter.cpp:6-15). Ids of other shards are skipped; ids
+ * outside [0, vocab_size) are skipped and set NIMBLE_STATUS_BAD_LABEL. */
 NIMBLE_API int nimble_embedding_scatter_add(float* grad_weights, const int64_t* ids, const void* grad_out,
-                                            int64_t n_rows, int64_t vocab, int64_t d_model,
-                                            int grad_out_dtype, int* status, void* stream);
+                                            int64_t n_rows, int64_t vocab_offset, int64_t vocab_rows,
+                                            int64_t vocab_size, int64_t d_model, int grad_out_dtype,
+                                            void* workspace, size_t workspace_bytes, int* status,
+                                            void* stream);
 
 /* One AdamW step over n fp32 master weights (NimbleML/optimizers/adam.py:20-43,
  * the fused update used for each parameter, e.g. a vocab shard of E):

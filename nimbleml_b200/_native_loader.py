@@ -85,10 +85,12 @@ SIGNATURES = {
     "nimble_rmsnorm_backward_workspace_size": (_c_int, [_c_i64, _c_i64, ctypes.POINTER(_c_size)]),
     "nimble_rmsnorm_backward": (
         _c_int,
-        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_float, _c_int, _c_vp, _c_vp,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_float, _c_int, _c_int, _c_vp, _c_vp,
          _c_int, _c_vp, _c_size, _c_vp]),
+    "nimble_embedding_scatter_add_workspace_size": (_c_int, [_c_i64, _c_i64, ctypes.POINTER(_c_size)]),
     "nimble_embedding_scatter_add": (
-        _c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_size, _c_vp, _c_vp]),
     "nimble_adamw_step": (
         _c_int,
         [_c_vp, _c_vp, _c_int, _c_vp, _c_vp, _c_i64] + [ctypes.c_float] * 7 + [_c_vp, _c_int, _c_vp]),
@@ -137,6 +139,11 @@ class NativeLibrary:
         out = _c_size(0)
         name = "nimble_tied_ce_backward_overlap_workspace_size" if overlap else "nimble_tied_ce_backward_workspace_size"
         self.call(name, n, d, v_local, dtype, slab_bytes, ctypes.byref(out))
+        return out.value
+
+    def scatter_add_workspace_size(self, n, vocab_rows) -> int:
+        out = _c_size(0)
+        self.call("nimble_embedding_scatter_add_workspace_size", n, vocab_rows, ctypes.byref(out))
         return out.value
 
     def rmsnorm_backward_workspace_size(self, n, d) -> int:

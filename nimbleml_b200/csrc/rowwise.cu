@@ -12,10 +12,13 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cub/device/device_radix_sort.cuh>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <string>
+#include <type_traits>
 
 #include "common.cuh"
 #include "nimbleml_tied_ce.h"
@@ -241,9 +244,11 @@ rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ gamma, int64_t
 
 // grad_x = grad*gamma/rms + x * (2/d) * (-1/2) * (sum_j grad_j gamma_j x_j) * (ms+eps)^(-3/2)
 // and, per block, partial sums over its rows of grad * x / rms for grad_gamma.
-template <typename T, int KMAX>
+// The incoming grad has its own type GT (fp32 when it comes straight from the
+// tied head's fp32 grad_hidden).
+template <typename T, typename GT, int KMAX>
 __global__ void __launch_bounds__(kNormThreads)
-rmsnorm_bwd_kernel(const T* __restrict__ grad, const T* __restrict__ x, const T* __restrict__ gamma,
+rmsnorm_bwd_kernel(const GT* __restrict__ grad, const T* __restrict__ x, const T* __restrict__ gamma,
                    const float* __restrict__ ms, const float* __restrict__ rms, int64_t N, int d, float eps,
                    T* __restrict__ gx, float* __restrict__ partial) {
   __shared__ float red[kNormThreads / 32];
@@ -260,7 +265,7 @@ rmsnorm_bwd_kernel(const T* __restrict__ grad, const T* __restrict__ x, const T*
 #pragma unroll
     for (int k = 0; k < KMAX; ++k) {
       const int j = threadIdx.x + k * kNormThreads;
-      gv[k] = j < d ? to_f<T>(grad[row * d + j]) : 0.0f;
+      gv[k] = j < d ? to_f<GT>(grad[row * d + j]) : 0.0f;
       xv[k] = j < d ? to_f<T>(x[row * d + j]) : 0.0f;
       dot = fmaf(gv[k] * gm[k], xv[k], dot);
     }
@@ -292,16 +297,41 @@ __global__ void sum_partials_kernel(const float* __restrict__ partial, int G, in
   out[j] = accumulate ? out[j] + s : s;
 }
 
+// Embedding scatter-add, deterministic: each row's id becomes a shard-local
+// sort key (ids of other shards and out-of-range ids get the sentinel
+// `v_local`), a stable radix sort groups equal keys with their rows in
+// ascending order, and one block per group adds those rows to the grad row in
+// that order — the loop order of the reference's CPU scatter
+// (native/src/scatter.cpp:6-15), so fp32 results do not depend on scheduling.
+__global__ void scatter_keys_kernel(const int64_t* __restrict__ ids, int64_t n, int64_t v_off, int64_t v_local,
+                                    int64_t vocab, uint32_t* __restrict__ keys, int32_t* __restrict__ rows,
+                                    int* status) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t id = ids[i];
+    if ((id < 0 || id >= vocab) && status) atomicOr(status, NIMBLE_STATUS_BAD_LABEL);
+    const int64_t local = id - v_off;
+    keys[i] = (id >= 0 && id < vocab && local >= 0 && local < v_local) ? static_cast<uint32_t>(local)
+                                                                       : static_cast<uint32_t>(v_local);
+    rows[i] = static_cast<int32_t>(i);
+  }
+}
+
 template <typename T>
-__global__ void scatter_add_kernel(float* __restrict__ gw, const int64_t* __restrict__ ids,
-                                   const T* __restrict__ go, int64_t N, int64_t V, int d, int* status) {
-  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
-    const int64_t id = ids[row];
-    if (id < 0 || id >= V) {
-      if (threadIdx.x == 0 && status) atomicOr(status, NIMBLE_STATUS_BAD_LABEL);
-      continue;
+__global__ void scatter_segments_kernel(float* __restrict__ gw, const uint32_t* __restrict__ keys,
+                                        const int32_t* __restrict__ rows, const T* __restrict__ go, int64_t n,
+                                        uint32_t sentinel, int d) {
+  for (int64_t b = blockIdx.x; b < n; b += gridDim.x) {
+    const uint32_t key = keys[b];
+    if (key == sentinel || (b > 0 && keys[b - 1] == key)) continue;  // not the first row of a group
+    int64_t e = b + 1;
+    while (e < n && keys[e] == key) ++e;
+    float* dst = gw + static_cast<int64_t>(key) * d;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+      float acc = dst[j];
+      for (int64_t p = b; p < e; ++p) acc += to_f<T>(go[static_cast<int64_t>(rows[p]) * d + j]);
+      dst[j] = acc;
     }
-    for (int j = threadIdx.x; j < d; j += blockDim.x) atomicAdd(gw + id * d + j, to_f<T>(go[row * d + j]));
   }
 }
 
@@ -474,9 +504,9 @@ extern "C" int nimble_rmsnorm_backward_workspace_size(int64_t n_rows, int64_t d_
 
 extern "C" int nimble_rmsnorm_backward(const void* grad, const void* x, const void* gamma, const float* ms,
                                        const float* rms, int64_t n_rows, int64_t d_model, float eps, int dtype,
-                                       void* grad_x, float* grad_gamma, int accumulate_grad_gamma, void* workspace,
-                                       size_t workspace_bytes, void* stream) {
-  if (!valid_dtype(dtype)) return fail(NIMBLE_ERR_INVALID_ARG, "bad dtype");
+                                       int grad_dtype, void* grad_x, float* grad_gamma, int accumulate_grad_gamma,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (!valid_dtype(dtype) || !valid_dtype(grad_dtype)) return fail(NIMBLE_ERR_INVALID_ARG, "bad dtype");
   if (n_rows < 0 || d_model <= 0 || d_model > kNormMaxD)
     return fail(NIMBLE_ERR_INVALID_ARG, "need n_rows >= 0 and 0 < d_model <= 8192");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -491,17 +521,26 @@ extern "C" int nimble_rmsnorm_backward(const void* grad, const void* x, const vo
   if (!workspace || workspace_bytes < sizeof(float) * static_cast<size_t>(grid) * d)
     return fail(NIMBLE_ERR_WORKSPACE, "rmsnorm backward workspace too small");
   float* partial = static_cast<float*>(workspace);
+  // The incoming grad is either in the compute dtype or fp32.
+  if (grad_dtype != dtype && grad_dtype != NIMBLE_DTYPE_F32)
+    return fail(NIMBLE_ERR_INVALID_ARG, "grad_dtype must be the compute dtype or NIMBLE_DTYPE_F32");
   NIMBLE_DISPATCH(dtype, T, {
-    const T* gt = static_cast<const T*>(grad);
     const T* xt = static_cast<const T*>(x);
     const T* gm = static_cast<const T*>(gamma);
     T* gxt = static_cast<T*>(grad_x);
-    if (d <= 4 * kNormThreads)
-      rmsnorm_bwd_kernel<T, 4><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
-    else if (d <= 16 * kNormThreads)
-      rmsnorm_bwd_kernel<T, 16><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
+    auto launch = [&](auto gt) {
+      using GT = std::remove_cv_t<std::remove_pointer_t<decltype(gt)>>;
+      if (d <= 4 * kNormThreads)
+        rmsnorm_bwd_kernel<T, GT, 4><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
+      else if (d <= 16 * kNormThreads)
+        rmsnorm_bwd_kernel<T, GT, 16><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
+      else
+        rmsnorm_bwd_kernel<T, GT, 32><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
+    };
+    if (grad_dtype == NIMBLE_DTYPE_F32)
+      launch(static_cast<const float*>(grad));
     else
-      rmsnorm_bwd_kernel<T, 32><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
+      launch(static_cast<const T*>(grad));
   });
   NIMBLE_CUDA_TRY(cudaGetLastError());
   sum_partials_kernel<<<(d + 255) / 256, 256, 0, s>>>(partial, grid, d, grad_gamma, accumulate_grad_gamma);
@@ -510,19 +549,81 @@ extern "C" int nimble_rmsnorm_backward(const void* grad, const void* x, const vo
 }
 
 // ------------------------------------------------ embedding grad and AdamW
+namespace {
+// Workspace of the scatter-add: keys and row indices in and out of the
+// stable radix sort, then the sort's own temporary storage.
+struct ScatterLayout {
+  size_t keys_in = 0, keys_out = 0, rows_in = 0, rows_out = 0, temp = 0, temp_bytes = 0, total = 0;
+};
+int key_bits(int64_t v_local) {
+  int bits = 1;
+  while ((int64_t(1) << bits) <= v_local) ++bits;  // keys 0..v_local inclusive
+  return bits;
+}
+int scatter_layout(int64_t n, int64_t v_local, ScatterLayout* L) {
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  size_t off = 0;
+  L->keys_in = off; off = up(off + sizeof(uint32_t) * n);
+  L->keys_out = off; off = up(off + sizeof(uint32_t) * n);
+  L->rows_in = off; off = up(off + sizeof(int32_t) * n);
+  L->rows_out = off; off = up(off + sizeof(int32_t) * n);
+  size_t temp = 0;
+  NIMBLE_CUDA_TRY(cub::DeviceRadixSort::SortPairs(nullptr, temp, static_cast<const uint32_t*>(nullptr),
+                                                  static_cast<uint32_t*>(nullptr), static_cast<const int32_t*>(nullptr),
+                                                  static_cast<int32_t*>(nullptr), static_cast<int>(n), 0,
+                                                  key_bits(v_local)));
+  L->temp = off;
+  L->temp_bytes = temp;
+  off = up(off + temp);
+  L->total = off;
+  return NIMBLE_OK;
+}
+}  // namespace
+
+extern "C" int nimble_embedding_scatter_add_workspace_size(int64_t n_rows, int64_t vocab_rows, size_t* bytes) {
+  if (!bytes || n_rows < 0 || n_rows > INT32_MAX || vocab_rows <= 0 || vocab_rows >= INT32_MAX)
+    return fail(NIMBLE_ERR_INVALID_ARG, "need 0 <= n_rows < 2^31, 0 < vocab_rows < 2^31 and a bytes pointer");
+  ScatterLayout L;
+  if (n_rows == 0) {
+    *bytes = 0;
+    return NIMBLE_OK;
+  }
+  if (int rc = scatter_layout(n_rows, vocab_rows, &L)) return rc;
+  *bytes = L.total;
+  return NIMBLE_OK;
+}
+
 extern "C" int nimble_embedding_scatter_add(float* grad_weights, const int64_t* ids, const void* grad_out,
-                                            int64_t n_rows, int64_t vocab, int64_t d_model, int grad_out_dtype,
-                                            int* status, void* stream) {
+                                            int64_t n_rows, int64_t vocab_offset, int64_t vocab_rows,
+                                            int64_t vocab_size, int64_t d_model, int grad_out_dtype,
+                                            void* workspace, size_t workspace_bytes, int* status, void* stream) {
   if (!valid_dtype(grad_out_dtype)) return fail(NIMBLE_ERR_INVALID_ARG, "bad dtype");
-  if (n_rows < 0 || vocab <= 0 || d_model <= 0 || d_model > INT32_MAX) return fail(NIMBLE_ERR_INVALID_ARG, "bad sizes");
+  if (n_rows < 0 || n_rows > INT32_MAX || vocab_rows <= 0 || vocab_rows >= INT32_MAX || vocab_size <= 0 ||
+      vocab_offset < 0 || vocab_offset + vocab_rows > vocab_size || d_model <= 0 || d_model > INT32_MAX)
+    return fail(NIMBLE_ERR_INVALID_ARG, "bad sizes");
   if (n_rows == 0) return NIMBLE_OK;
   if (!grad_weights || !ids || !grad_out) return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
+  ScatterLayout L;
+  if (int rc = scatter_layout(n_rows, vocab_rows, &L)) return rc;
+  if (!workspace || workspace_bytes < L.total) return fail(NIMBLE_ERR_WORKSPACE, "scatter-add workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint32_t* keys_in = reinterpret_cast<uint32_t*>(ws + L.keys_in);
+  uint32_t* keys_out = reinterpret_cast<uint32_t*>(ws + L.keys_out);
+  int32_t* rows_in = reinterpret_cast<int32_t*>(ws + L.rows_in);
+  int32_t* rows_out = reinterpret_cast<int32_t*>(ws + L.rows_out);
+  scatter_keys_kernel<<<grid_for(n_rows, 256), 256, 0, s>>>(ids, n_rows, vocab_offset, vocab_rows, vocab_size, keys_in,
+                                                            rows_in, status);
+  NIMBLE_CUDA_TRY(cudaGetLastError());
+  size_t temp = L.temp_bytes;
+  NIMBLE_CUDA_TRY(cub::DeviceRadixSort::SortPairs(ws + L.temp, temp, keys_in, keys_out, rows_in, rows_out,
+                                                  static_cast<int>(n_rows), 0, key_bits(vocab_rows), s));
   const int grid = static_cast<int>(std::min<int64_t>(n_rows, 148 * 16));
   const int threads = d_model >= 256 ? 256 : 128;
   NIMBLE_DISPATCH(grad_out_dtype, T,
-                  scatter_add_kernel<T><<<grid, threads, 0, s>>>(grad_weights, ids, static_cast<const T*>(grad_out),
-                                                                 n_rows, vocab, static_cast<int>(d_model), status));
+                  scatter_segments_kernel<T><<<grid, threads, 0, s>>>(
+                      grad_weights, keys_out, rows_out, static_cast<const T*>(grad_out), n_rows,
+                      static_cast<uint32_t>(vocab_rows), static_cast<int>(d_model)));
   NIMBLE_CUDA_TRY(cudaGetLastError());
   return NIMBLE_OK;
 }

@@ -2,7 +2,8 @@
 
 * ``embedding_scatter_add`` — grad_weights[ids] += grad_out, the input
   embedding's share of the tied matrix's grad
-  (NimbleML/kernels/embedding_scatter.py:39-81), into an fp32 grad buffer.
+  (NimbleML/kernels/embedding_scatter.py:39-81), into an fp32 grad buffer,
+  deterministically and for one vocab shard.
 * ``AdamW`` — the reference's fused AdamW update (NimbleML/optimizers/adam.py:20-43,
   85-131, 295-312) over fp32 master weights, e.g. one rank's vocab shard of E,
   with an optional low-precision copy written in the same pass.
@@ -16,18 +17,32 @@ import torch
 from nimbleml_b200.kernels.fused_tied_crossentropy import _TORCH_TO_NIMBLE, _stream_ptr, native, status_word
 
 
-def embedding_scatter_add(grad_weights: torch.Tensor, ids: torch.Tensor, grad_out: torch.Tensor) -> torch.Tensor:
-    """In-place ``grad_weights[ids[i]] += grad_out[i]`` (fp32 grad_weights, repeats summed)."""
+def embedding_scatter_add(grad_weights: torch.Tensor, ids: torch.Tensor, grad_out: torch.Tensor, *,
+                          vocab_offset: int = 0, vocab_size: Optional[int] = None) -> torch.Tensor:
+    """In-place ``grad_weights[ids[i] - vocab_offset] += grad_out[i]`` into an fp32 grad.
+
+    ``grad_weights`` holds rows [vocab_offset, vocab_offset + rows) of a
+    ``vocab_size`` vocabulary (default: all of it); ids of other rows are
+    skipped, ids outside [0, vocab_size) set the status word's bad-label bit.
+    Deterministic: each id's rows are added in ascending row order, the loop
+    order of the reference's CPU scatter (native/src/scatter.cpp:6-15).
+    """
     if grad_weights.dtype != torch.float32 or not grad_weights.is_contiguous():
         raise ValueError("grad_weights must be a contiguous float32 (vocab, d) tensor")
     v, d = grad_weights.shape
+    vocab_size = v if vocab_size is None else int(vocab_size)
     flat_ids = ids.reshape(-1).to(torch.int64).contiguous()
     go = grad_out.reshape(-1, d).contiguous()
-    if go.shape[0] != flat_ids.numel():
-        raise ValueError(f"ids length ({flat_ids.numel()}) must match grad_out rows ({go.shape[0]}).")
-    native.call("nimble_embedding_scatter_add", grad_weights.data_ptr(), flat_ids.data_ptr(), go.data_ptr(),
-                go.shape[0], v, d, _TORCH_TO_NIMBLE[go.dtype], status_word(go.device).data_ptr(),
-                _stream_ptr(go.device))
+    n = go.shape[0]
+    if n != flat_ids.numel():
+        raise ValueError(f"ids length ({flat_ids.numel()}) must match grad_out rows ({n}).")
+    if n == 0:
+        return grad_weights
+    ws_bytes = native.scatter_add_workspace_size(n, v)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=go.device)
+    native.call("nimble_embedding_scatter_add", grad_weights.data_ptr(), flat_ids.data_ptr(), go.data_ptr(), n,
+                int(vocab_offset), v, vocab_size, d, _TORCH_TO_NIMBLE[go.dtype], ws.data_ptr(), ws_bytes,
+                status_word(go.device).data_ptr(), _stream_ptr(go.device))
     return grad_weights
 
 

@@ -42,64 +42,101 @@ from nimbleml_b200.kernels.fused_tied_crossentropy import (
 )
 
 
+def tied_forward_core(h2d, weights, labels, ignore_index, vocab_offset, vocab_size, group):
+    """Forward of the tied head + CE for one vocab shard (shared by the autograd nodes).
+
+    Returns ``(loss, saved)``: the fp32 0-d loss and what ``tied_backward_core``
+    needs — the operands in the compute dtype, the labels, the per-token lse
+    and valid count, and (fp32) the TF32-rounded operand copies.
+    """
+    from nimbleml_b200 import vocab_parallel
+
+    # The tensor cores read E in the hidden's dtype; fp32 master weights
+    # are cast for the GEMMs but receive an fp32 grad straight from the
+    # kernel epilogue.
+    weights_in_dtype = weights.dtype
+    if weights.dtype != h2d.dtype:
+        weights = weights.to(h2d.dtype)
+    weights = weights.contiguous()
+    rounded = (round_tf32(h2d), round_tf32(weights)) if h2d.dtype == torch.float32 else None
+    part = shard_forward(*(rounded or (h2d, weights)), labels, vocab_offset, rounded=rounded is not None)
+    stats3 = vocab_parallel.gather_shard_stats(part, group)  # (3, P, N)
+    _, _, lse, loss, valid = combine(stats3, labels, vocab_size, ignore_index)
+    if CHECK_BOUNDS:
+        check_status(h2d.device)
+    saved = dict(h2d=h2d, weights=weights, labels=labels, lse=lse, valid=valid, rounded=rounded,
+                 meta=(ignore_index, vocab_offset, vocab_size, group, weights_in_dtype))
+    return loss, saved
+
+
+def tied_backward_core(grad_out, saved, *, grad_buffer=None, grad_hidden_dtype=None):
+    """(grad_hidden, grad_weights or None) of ``tied_forward_core``'s loss.
+
+    With ``grad_buffer`` the shard's dE is added into it by the GEMM epilogue
+    and None is returned for the weights. ``grad_hidden_dtype`` defaults to
+    the compute dtype.
+    """
+    from nimbleml_b200 import vocab_parallel
+
+    h2d, weights, labels = saved["h2d"], saved["weights"], saved["labels"]
+    ignore_index, vocab_offset, vocab_size, group, w_dtype = saved["meta"]
+    stats = TiedCEStats(lse=saved["lse"], valid_count=saved["valid"], ignore_index=ignore_index,
+                        vocab_size=vocab_size, vocab_offset=vocab_offset, rounded=saved["rounded"])
+    grad_w = grad_buffer if grad_buffer is not None else torch.empty(weights.shape, dtype=w_dtype,
+                                                                     device=weights.device)
+    gh_dtype = grad_hidden_dtype or h2d.dtype
+    if vocab_parallel.world_size(group) > 1:
+        grad_h, grad_w = vocab_parallel.sharded_backward(grad_out, h2d, weights, labels, stats, group,
+                                                         grad_weights=grad_w, accumulate=grad_buffer is not None)
+        if grad_h.dtype != gh_dtype:
+            grad_h = grad_h.to(gh_dtype)
+    else:
+        grad_h, grad_w = shard_backward(grad_out, h2d, weights, labels, stats, grad_weights=grad_w,
+                                        accumulate=grad_buffer is not None, grad_hidden_dtype=gh_dtype)
+    if CHECK_BOUNDS:
+        check_status(h2d.device)
+    return grad_h, (None if grad_buffer is not None else grad_w)
+
+
 class _TiedCrossEntropy(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, h2d, weights, labels, ignore_index, vocab_offset, vocab_size, group):
-        from nimbleml_b200 import vocab_parallel
-
-        # The tensor cores read E in the hidden's dtype; fp32 master weights
-        # are cast for the GEMMs but receive an fp32 grad straight from the
-        # kernel epilogue.
-        weights_in_dtype = weights.dtype
-        if weights.dtype != h2d.dtype:
-            weights = weights.to(h2d.dtype)
-        weights = weights.contiguous()
-        rounded = (round_tf32(h2d), round_tf32(weights)) if h2d.dtype == torch.float32 else None
-        part = shard_forward(*(rounded or (h2d, weights)), labels, vocab_offset, rounded=rounded is not None)
-        stats3 = vocab_parallel.gather_shard_stats(part, group)  # (3, P, N)
-        _, _, lse, loss, valid = combine(stats3, labels, vocab_size, ignore_index)
-        if CHECK_BOUNDS:
-            check_status(h2d.device)
-        ctx.save_for_backward(h2d, weights, labels, lse, valid)
-        ctx.rounded = rounded
-        ctx.meta = (ignore_index, vocab_offset, vocab_size, group, weights_in_dtype)
+    def forward(ctx, h2d, weights, labels, ignore_index, vocab_offset, vocab_size, group, grad_buffer=None):
+        loss, ctx.saved = tied_forward_core(h2d, weights, labels, ignore_index, vocab_offset, vocab_size, group)
+        ctx.grad_buffer = grad_buffer
         return loss
 
     @staticmethod
     def backward(ctx, grad_out):
-        from nimbleml_b200 import vocab_parallel
-
-        h2d, weights, labels, lse, valid = ctx.saved_tensors
-        ignore_index, vocab_offset, vocab_size, group, w_dtype = ctx.meta
-        stats = TiedCEStats(lse=lse, valid_count=valid, ignore_index=ignore_index,
-                            vocab_size=vocab_size, vocab_offset=vocab_offset, rounded=ctx.rounded)
-        ctx.rounded = None
-        sharded = vocab_parallel.world_size(group) > 1
-        grad_w = torch.empty(weights.shape, dtype=w_dtype, device=weights.device)
-        if sharded:
-            grad_h, grad_w = vocab_parallel.sharded_backward(grad_out, h2d, weights, labels, stats, group,
-                                                             grad_weights=grad_w)
-            grad_h = grad_h.to(h2d.dtype)
-        else:
-            grad_h, grad_w = shard_backward(grad_out, h2d, weights, labels, stats, grad_weights=grad_w)
-        if CHECK_BOUNDS:
-            check_status(h2d.device)
-        return grad_h, grad_w, None, None, None, None, None
+        saved, buf = ctx.saved, ctx.grad_buffer
+        ctx.saved = ctx.grad_buffer = None
+        grad_h, grad_w = tied_backward_core(grad_out, saved, grad_buffer=buf)
+        return grad_h, grad_w, None, None, None, None, None, None
 
 
 def tied_cross_entropy(hidden2d, weights, labels, ignore_index: Optional[int] = None, *,
-                       vocab_offset: int = 0, vocab_size: Optional[int] = None, group=None):
+                       vocab_offset: int = 0, vocab_size: Optional[int] = None, group=None,
+                       grad_weights_buffer: Optional[torch.Tensor] = None):
     """Functional form: mean CE of ``hidden2d @ weights^T`` against ``labels``.
 
     With ``group`` set (a torch.distributed process group), ``weights`` is
     this rank's vocab shard starting at class ``vocab_offset`` of a
     ``vocab_size`` vocabulary; every rank gets the same loss, the grad of its
     own shard and the full ``hidden`` grad.
+
+    ``grad_weights_buffer``: an fp32 tensor of the weights' shape that the
+    backward adds this loss's weight grad into (the tied matrix's one grad
+    buffer, shared with the embedding lookup's scatter-add); autograd then
+    gets no grad for ``weights``.
     """
     ign = _NO_IGNORE if ignore_index is None else int(ignore_index)
     if vocab_size is None:
         vocab_size = weights.shape[0]
-    return _TiedCrossEntropy.apply(hidden2d, weights, labels, ign, int(vocab_offset), int(vocab_size), group)
+    if grad_weights_buffer is not None and (grad_weights_buffer.dtype != torch.float32 or
+                                            grad_weights_buffer.shape != weights.shape or
+                                            not grad_weights_buffer.is_contiguous()):
+        raise ValueError("grad_weights_buffer must be a contiguous float32 tensor of the weights' shape")
+    return _TiedCrossEntropy.apply(hidden2d, weights, labels, ign, int(vocab_offset), int(vocab_size), group,
+                                   grad_weights_buffer)
 
 
 def _flatten_logits(logits):

@@ -18,12 +18,7 @@ class _RMSNormFn(torch.autograd.Function):
         d = x.shape[-1]
         x2d = x.reshape(-1, d).contiguous()
         g = gamma.to(x.dtype).contiguous()
-        n = x2d.shape[0]
-        y = torch.empty_like(x2d)
-        ms = torch.empty(n, dtype=torch.float32, device=x.device)
-        rms = torch.empty(n, dtype=torch.float32, device=x.device)
-        native.call("nimble_rmsnorm_forward", x2d.data_ptr(), g.data_ptr(), n, d, float(eps),
-                    _TORCH_TO_NIMBLE[x.dtype], y.data_ptr(), ms.data_ptr(), rms.data_ptr(), _stream_ptr(x.device))
+        y, ms, rms = rmsnorm_forward(x2d, g, eps)
         ctx.save_for_backward(x2d, g, ms, rms)
         ctx.eps = float(eps)
         ctx.gamma_dtype = gamma.dtype
@@ -33,15 +28,37 @@ class _RMSNormFn(torch.autograd.Function):
     def backward(ctx, grad):
         x2d, g, ms, rms = ctx.saved_tensors
         n, d = x2d.shape
-        gy = grad.reshape(n, d).to(x2d.dtype).contiguous()
-        gx = torch.empty_like(x2d)
-        gg = torch.empty(d, dtype=torch.float32, device=x2d.device)
-        ws_bytes = native.rmsnorm_backward_workspace_size(n, d)
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x2d.device)
-        native.call("nimble_rmsnorm_backward", gy.data_ptr(), x2d.data_ptr(), g.data_ptr(), ms.data_ptr(),
-                    rms.data_ptr(), n, d, ctx.eps, _TORCH_TO_NIMBLE[x2d.dtype], gx.data_ptr(), gg.data_ptr(), 0,
-                    ws.data_ptr(), ws_bytes, _stream_ptr(x2d.device))
+        gx, gg = rmsnorm_backward(grad.reshape(n, d), x2d, g, ms, rms, ctx.eps)
         return gx.view(grad.shape), gg.to(ctx.gamma_dtype), None
+
+
+def rmsnorm_forward(x2d: torch.Tensor, gamma: torch.Tensor, eps: float):
+    """(y, ms, rms) of nimble_rmsnorm_forward for a contiguous (n, d) input; gamma in x's dtype."""
+    n, d = x2d.shape
+    y = torch.empty_like(x2d)
+    ms = torch.empty(n, dtype=torch.float32, device=x2d.device)
+    rms = torch.empty(n, dtype=torch.float32, device=x2d.device)
+    native.call("nimble_rmsnorm_forward", x2d.data_ptr(), gamma.data_ptr(), n, d, float(eps),
+                _TORCH_TO_NIMBLE[x2d.dtype], y.data_ptr(), ms.data_ptr(), rms.data_ptr(), _stream_ptr(x2d.device))
+    return y, ms, rms
+
+
+def rmsnorm_backward(grad2d: torch.Tensor, x2d: torch.Tensor, gamma: torch.Tensor, ms: torch.Tensor,
+                     rms: torch.Tensor, eps: float):
+    """(grad_x in x's dtype, grad_gamma fp32). An fp32 ``grad2d`` is read as is
+    (the tied head's fp32 grad_hidden); other dtypes are cast to x's dtype."""
+    n, d = x2d.shape
+    if grad2d.dtype != torch.float32 and grad2d.dtype != x2d.dtype:
+        grad2d = grad2d.to(x2d.dtype)
+    gy = grad2d.contiguous()
+    gx = torch.empty_like(x2d)
+    gg = torch.empty(d, dtype=torch.float32, device=x2d.device)
+    ws_bytes = native.rmsnorm_backward_workspace_size(n, d)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x2d.device)
+    native.call("nimble_rmsnorm_backward", gy.data_ptr(), x2d.data_ptr(), gamma.data_ptr(), ms.data_ptr(),
+                rms.data_ptr(), n, d, float(eps), _TORCH_TO_NIMBLE[x2d.dtype], _TORCH_TO_NIMBLE[gy.dtype],
+                gx.data_ptr(), gg.data_ptr(), 0, ws.data_ptr(), ws_bytes, _stream_ptr(x2d.device))
+    return gx, gg
 
 
 def rms_norm(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
@@ -67,4 +84,4 @@ class RMSNorm(torch.nn.Module):
         return rms_norm(inputs, self.gamma, self.epsilon)
 
 
-__all__ = ["RMSNorm", "rms_norm"]
+__all__ = ["RMSNorm", "rms_norm", "rmsnorm_forward", "rmsnorm_backward"]

@@ -15,8 +15,8 @@ inputs and outputs of
 as ``.npz`` files beside this script. Run in a container that has the
 reference checkout (it is not needed afterwards):
 
-    make -C oracle REF=/root/reference
-    python tests/golden/gen_golden.py --ref /root/reference
+    make -C oracle REF=<reference checkout>
+    python tests/golden/gen_golden.py --ref <reference checkout>
 """
 from __future__ import annotations
 
@@ -208,12 +208,89 @@ def row_kernels_case(nb):
     return "row_kernels_f32", out
 
 
+def tied_embedding_case(nb):
+    """The tied matrix used twice — input embedding lookup and tied LM head —
+    through the reference's Embedding (NimbleML/layers/embedding.py:23-67,138-148),
+    forward_tied (NimbleML/losses/cross_entropy.py:109-192) and one AdamW step
+    (NimbleML/optimizers/adam.py:85-131,295-312), fp32. E.grad is the head's dE
+    plus the lookup's scatter-add (with repeated ids)."""
+    from NimbleML.layers import Embedding
+    from NimbleML.losses.cross_entropy import CrossEntropyLoss
+    from NimbleML.optimizers import AdamW
+    from NimbleML.utils.tensor import Tensor
+
+    nb.set_dtype("float32")
+    np.random.seed(5)
+    v, d, b, s = 300, 64, 4, 32
+    emb = Embedding(v, d, init_std=0.5)
+    rng = np.random.default_rng(6)
+    ids = rng.integers(0, v, (b, s), dtype=np.int64)
+    ids[:, ::4] = 7  # a frequent token: many rows scatter into one grad row
+    labels = rng.integers(0, v, (b, s), dtype=np.int64)
+    labels[0, :5] = -1
+    e0 = np.asarray(emb.weights._view()).astype(np.float32).copy()
+    h = emb(Tensor.from_int64(ids, (b, s)))
+    loss = CrossEntropyLoss().forward_tied(h, emb.weights, labels, ignore_index=-1)
+    loss.backward()
+    grad = np.asarray(emb.weights.grad).reshape(v, d).astype(np.float32).copy()
+    lr, b1, b2, eps, wd = 1e-3, 0.9, 0.999, 1e-8, 0.01
+    opt = AdamW([emb.weights], learning_rate=lr, beta1=b1, beta2=b2, epsilon=eps, weight_decay=wd)
+    opt.step()
+    e1 = np.asarray(emb.weights._view()).astype(np.float32).copy()
+    return "tied_embedding_adamw_f32", {"ids": ids, "labels": labels.ravel(), "e0": e0, "grad": grad, "e1": e1,
+                                        "loss": loss.item(), "lr": lr, "b1": b1, "b2": b2, "eps": eps, "wd": wd}
+
+
+def norm_head_case(nb):
+    """The final RMSNorm feeding the tied head (NimbleML/models/gpt.py:67,90,
+    NimbleML/layers/rms_norm.py:25-95) then forward_tied, fp32: loss and the
+    grads of x, gamma and E."""
+    from NimbleML.layers import RMSNorm
+    from NimbleML.losses.cross_entropy import CrossEntropyLoss
+    from NimbleML.utils.tensor import Tensor
+
+    nb.set_dtype("float32")
+    np.random.seed(8)
+    v, d, b, s = 500, 128, 3, 40
+    norm = RMSNorm(d)
+    rng = np.random.default_rng(9)
+    norm.gamma.data[...] = (1.0 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    x = (2.0 * rng.standard_normal((b, s, d))).astype(np.float32)
+    e = (0.05 * rng.standard_normal((v, d))).astype(np.float32)
+    labels = rng.integers(0, v, (b, s), dtype=np.int64)
+    xt = Tensor(x.ravel(), (b, s, d), requires_grad=True)
+    et = Tensor(e.ravel(), (v, d), requires_grad=True)
+    loss = CrossEntropyLoss().forward_tied(norm(xt), et, labels)
+    loss.backward()
+    return "norm_head_f32", {"x": x, "e": e, "gamma": np.asarray(norm.gamma.data).astype(np.float32).copy(),
+                             "labels": labels.ravel(), "loss": loss.item(), "eps": norm.epsilon,
+                             "dx": np.asarray(xt.grad).reshape(b, s, d), "de": np.asarray(et.grad).reshape(v, d),
+                             "dgamma": np.asarray(norm.gamma.grad).reshape(d)}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("NIMBLEML_REFERENCE"),
+                    help="the reference checkout (or set NIMBLEML_REFERENCE)")
+    ap.add_argument("--only", nargs="*", help="write only these fixtures (file stems)")
     args = ap.parse_args()
+    if not args.ref or not (Path(args.ref) / "NimbleML").is_dir():
+        raise SystemExit("pass --ref <reference checkout> (or set NIMBLEML_REFERENCE); its native extension must "
+                         "be built into oracle/_ref first: make -C oracle REF=<checkout>")
     nb = _import_reference(Path(args.ref))
+    if args.only:
+        makers = {"tied_embedding_adamw_f32": tied_embedding_case, "norm_head_f32": norm_head_case,
+                  "c1_tiny_gpt": tiny_gpt_case, "tied_logits_c1": tied_logits_case,
+                  "row_kernels_f32": row_kernels_case}
+        for stem in args.only:
+            name, data = makers[stem](nb)
+            path = HERE / f"{name}.npz"
+            np.savez_compressed(path, **{k: np.asarray(v) for k, v in data.items()})
+            print(f"{path.name}: {path.stat().st_size / 1024:.0f} KiB, loss={float(data['loss']):.6f}")
+        return
     cases = [
+        tied_embedding_case(nb),
+        norm_head_case(nb),
         tiny_gpt_case(nb),
         tied_logits_case(nb),
         row_kernels_case(nb),

@@ -128,3 +128,33 @@ def test_row_kernel_restatements_match_reference():
         w, m, v = orc.adamw_step(w, gr.astype(np.float64), m, v, 1e-2, 0.9, 0.999, 1 - 0.9 ** t,
                                  1 - 0.999 ** t, 1e-8, 0.1)
     assert rel(w, g["a_w2"]) < 1e-6
+
+
+def test_tied_embedding_composition_matches_reference():
+    """Lookup + tied head + scatter-add into one grad, then AdamW (reference Embedding /
+    forward_tied / AdamW), restated by the oracle in the reference's order."""
+    g = load("tied_embedding_adamw_f32")
+    e0, ids, y = g["e0"], g["ids"].reshape(-1), g["labels"]
+    h = e0[ids]
+    loss, dh, de_head = orc.forward_tied_loss_and_grads(h, e0, y, ignore_index=-1)
+    assert abs(loss - float(g["loss"])) < 1e-6 * float(g["loss"])
+    grad = orc.embedding_scatter_add(de_head.astype(np.float32), ids, dh.astype(np.float32))
+    assert rel(grad, g["grad"]) < 1e-5
+    w, m, v = orc.adamw_step(e0.astype(np.float64), g["grad"].astype(np.float64), 0.0, 0.0, float(g["lr"]),
+                             float(g["b1"]), float(g["b2"]), 1 - float(g["b1"]), 1 - float(g["b2"]),
+                             float(g["eps"]), float(g["wd"]))
+    assert rel(w, g["e1"]) < 1e-6
+
+
+def test_norm_head_composition_matches_reference():
+    """Final RMSNorm then the tied head (reference RMSNorm + forward_tied), restated."""
+    g = load("norm_head_f32")
+    d = g["x"].shape[-1]
+    x = g["x"].reshape(-1, d)
+    yv, ms, rms = orc.rmsnorm_forward(x, g["gamma"], float(g["eps"]))
+    loss, dy, de = orc.forward_tied_loss_and_grads(yv, g["e"], g["labels"])
+    assert abs(loss - float(g["loss"])) < 1e-6 * float(g["loss"])
+    assert rel(de, g["de"]) < 1e-5
+    dx, dgamma = orc.rmsnorm_backward(dy, x, g["gamma"], ms, rms, float(g["eps"]))
+    assert rel(dx, g["dx"].reshape(-1, d)) < 1e-5
+    assert rel(dgamma, g["dgamma"]) < 1e-5
