@@ -39,6 +39,8 @@ CONFIGS = {
                unit_rms=True, batch=16, seq=1024),
     "mid": dict(workload="profiling case: config-4 d with N=4096, V=32768 (inputs > L2)", n=4096, d=4096,
                 v=32768, dtype="float16", unit_rms=True, batch=1, seq=4096),
+    "mid_bf16": dict(workload="profiling case: config-4 d with N=4096, V=32768, bf16 (inputs > L2)", n=4096,
+                     d=4096, v=32768, dtype="bfloat16", unit_rms=True, batch=1, seq=4096),
     "c2": dict(workload="config 2: standalone fused tied CE fwd+bwd, fp32 on TF32", n=8192, d=768,
                v=50257, dtype="float32", unit_rms=False, batch=8, seq=1024),
 }
@@ -320,28 +322,34 @@ def sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss
 
 def run_c5(args):
     """Config 5: one GPT training step (24 layers, d=1024, 16 heads, seq 1024,
-    batch 8, V=50257, fp16 autocast) with the fused head, AdamW and
-    clip_grad_norm_(1.0); reports the head's share of step time and memory.
+    batch 8, V=50257, fp16 autocast) with clip_grad_norm(1.0) and AdamW;
+    reports the head's share of step time and memory.
 
     The trunk is a plain torch harness (embedding + learned positions,
-    pre-norm blocks with SDPA attention and a GELU MLP); the final RMSNorm and
-    the tied head + CE are this library's kernels. Random init, synthetic ids.
+    pre-norm blocks with SDPA attention and a GELU MLP). This library runs the
+    tied matrix E end to end — TiedEmbedding's lookup, the final RMSNorm fused
+    with the tied head + CE, the one fp32 E grad buffer shared by the head's
+    dE and the lookup's deterministic scatter-add — and the AdamW update of
+    every parameter (nimble_adamw_step over fp32 masters; E's fp16 copy is
+    rewritten in the same pass). The loss scale is a static 2^15. Random
+    init, synthetic ids.
     """
     import torch
     import torch.nn.functional as F
 
-    from nimbleml_b200.losses.cross_entropy import CrossEntropyLoss
-    from nimbleml_b200.norm import RMSNorm
+    from nimbleml_b200.embedding_grad import AdamW
+    from nimbleml_b200.gpt_head import TiedEmbedding, norm_tied_cross_entropy
 
     torch.manual_seed(0)
     dev = torch.device("cuda", 0)
     V, D, H, L, S, B = 50257, 1024, 16, 24, 1024, 8
+    loss_scale = 32768.0
 
     class Block(torch.nn.Module):
         def __init__(self):
             super().__init__()
-            self.n1 = RMSNorm(D, device=dev)
-            self.n2 = RMSNorm(D, device=dev)
+            self.n1 = torch.nn.RMSNorm(D, device=dev)
+            self.n2 = torch.nn.RMSNorm(D, device=dev)
             self.qkv = torch.nn.Linear(D, 3 * D, bias=False, device=dev)
             self.o = torch.nn.Linear(D, D, bias=False, device=dev)
             self.up = torch.nn.Linear(D, 4 * D, bias=False, device=dev)
@@ -356,37 +364,40 @@ def run_c5(args):
     class GPT(torch.nn.Module):
         def __init__(self):
             super().__init__()
-            self.tok = torch.nn.Parameter(torch.randn(V, D, device=dev) * 0.02)
+            self.emb = TiedEmbedding(torch.randn(V, D, device=dev) * 0.02, V, compute_dtype=torch.float16,
+                                     learning_rate=3e-4, weight_decay=0.01)
             self.pos = torch.nn.Parameter(torch.randn(S, D, device=dev) * 0.02)
             self.blocks = torch.nn.ModuleList([Block() for _ in range(L)])
-            self.ln = RMSNorm(D, device=dev)
-            self.ce = CrossEntropyLoss()
+            self.ln_gamma = torch.nn.Parameter(torch.ones(D, device=dev))
 
         def hidden(self, ids):
-            x = self.tok[ids] + self.pos
+            x = self.emb.lookup(ids).float() + self.pos
             for blk in self.blocks:
                 x = blk(x)
-            return self.ln(x.half())
+            return x.half()
 
         def compute_loss(self, ids, labels):
-            return self.ce.forward_tied(self.hidden(ids), self.tok, labels)
+            return self.emb.loss(self.hidden(ids), labels, norm_gamma=self.ln_gamma)
 
     model = GPT()
-    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.01, fused=True)
-    scaler = torch.amp.GradScaler("cuda")
+    params = list(model.parameters())
+    opt = AdamW(params, learning_rate=3e-4, weight_decay=0.01)
     gen = torch.Generator(device=dev).manual_seed(1)
     ids = torch.randint(0, V, (B, S), device=dev, generator=gen)
     labels = torch.randint(0, V, (B, S), device=dev, generator=gen)
 
     def step():
         opt.zero_grad(set_to_none=True)
+        model.emb.zero_grad()
         with torch.autocast("cuda", dtype=torch.float16):
             loss = model.compute_loss(ids, labels)
-        scaler.scale(loss).backward()
-        scaler.unscale_(opt)
-        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
-        scaler.step(opt)
-        scaler.update()
+        (loss * loss_scale).backward()
+        grads = [p.grad for p in params] + [model.emb.grad]
+        torch._foreach_mul_(grads, 1.0 / loss_scale)
+        total = torch.linalg.vector_norm(torch.stack(torch._foreach_norm(grads)))
+        torch._foreach_mul_(grads, torch.clamp(1.0 / (total + 1e-6), max=1.0))  # clip_grad_norm(1.0)
+        opt.step()
+        model.emb.step()
         return loss
 
     def timed(fn, k):
@@ -407,18 +418,26 @@ def run_c5(args):
     torch.cuda.synchronize()
     step_peak = torch.cuda.max_memory_allocated(dev)
 
-    h = model.hidden(ids).detach().requires_grad_(True)
-    w = model.tok.detach().clone().requires_grad_(True)
+    with torch.no_grad():
+        x = model.hidden(ids)
+    xh = x.detach().requires_grad_(True)
+    gamma = model.ln_gamma.detach().requires_grad_(True)
+    w = model.emb.weight
+    buf = torch.zeros_like(model.emb.grad)
 
     def head_ours():
-        h.grad = None
-        w.grad = None
-        model.ce.forward_tied(h, w, labels).backward()
+        xh.grad = None
+        gamma.grad = None
+        norm_tied_cross_entropy(xh, gamma, w, labels, grad_weights_buffer=buf).backward()
+
+    wt = w.detach().clone().requires_grad_(True)
 
     def head_torch():
-        h.grad = None
-        w.grad = None
-        logits = (h.view(-1, D) @ w.half().T).float()
+        xh.grad = None
+        wt.grad = None
+        gamma.grad = None
+        y = F.rms_norm(xh, (D,), gamma.half(), 1e-5)
+        logits = (y.view(-1, D) @ wt.T).float()
         F.cross_entropy(logits, labels.view(-1)).backward()
 
     def peak(fn):
@@ -437,15 +456,90 @@ def run_c5(args):
         "value": B * S / (step_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "dtype": "f16",
         "data": "synthetic, random init",
-        "config": {"workload": "config 5 harness: torch trunk + this library's RMSNorm and fused tied head",
-                   "vocab": V, "d_model": D, "layers": L, "heads": H, "batch": B, "seq_len": S},
+        "config": {"workload": "config 5 harness: torch trunk; this library's tied embedding (lookup, shared fp32 "
+                               "grad, deterministic scatter), final RMSNorm fused with the tied head, AdamW",
+                   "vocab": V, "d_model": D, "layers": L, "heads": H, "batch": B, "seq_len": S,
+                   "loss_scale": loss_scale},
         "head": {"ms_fwd_bwd": head_ms, "share_of_step": head_ms / step_ms,
+                 "what": "final RMSNorm + tied head + CE, forward and backward",
                  "peak_extra_bytes": int(peak(head_ours)),
                  "materialised_torch_head_ms": torch_ms,
                  "materialised_torch_head_peak_extra_bytes": int(peak(head_torch)),
                  "head_tflops": 8.0 * B * S * D * V / (head_ms / 1e3) / 1e12},
         "step_peak_bytes": int(step_peak),
     }
+    print(json.dumps(line), flush=True)
+
+
+def run_rows(args):
+    """HBM-bound row kernels around the head: achieved GB/s (algorithmic bytes
+    per launch / CUDA-event time per launch, inputs larger than L2) against
+    the measured copy bandwidth. Not the headline metric."""
+    import torch
+
+    from nimbleml_b200.embedding_grad import embedding_scatter_add
+    from nimbleml_b200.kernels import fused_tied_crossentropy as k
+    from nimbleml_b200.losses.cross_entropy import CrossEntropyLoss
+    from nimbleml_b200.norm import rmsnorm_backward, rmsnorm_forward
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _, _, hbm, peak_kind = _peaks()
+    g = torch.Generator(device=dev).manual_seed(3)
+    out = {}
+
+    def timed(fn, nbytes, name, reps=None):
+        reps = args.rows_reps if reps is None else min(reps, args.rows_reps)
+        for _ in range(min(3, reps)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        out[name] = {"ms": ms, "bytes": int(nbytes), "gb_s": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / hbm}
+
+    n, d = 32768, 4096
+    x = torch.randn((n, d), generator=g, device=dev).half()
+    gamma = (1 + 0.1 * torch.randn(d, generator=g, device=dev)).half()
+    y, ms_, rms = rmsnorm_forward(x, gamma, 1e-5)
+    timed(lambda: rmsnorm_forward(x, gamma, 1e-5), 2 * n * d * 2 + 8 * n, "rmsnorm_forward f16 32768x4096")
+    gy = torch.randn((n, d), generator=g, device=dev)
+    timed(lambda: rmsnorm_backward(gy, x, gamma, ms_, rms, 1e-5), n * d * (4 + 2 + 2) + 8 * n,
+          "rmsnorm_backward fp32 grad -> f16 grad_x 32768x4096")
+    del y, gy
+    nl, vl = 8192, 50257
+    logits = torch.randn((nl, vl), generator=g, device=dev).half()
+    lab = torch.randint(0, vl, (nl,), generator=g, device=dev)
+    ce = CrossEntropyLoss()
+    timed(lambda: ce(logits, lab), nl * vl * 2, "ce_logits_forward f16 8192x50257")
+    lg = logits.detach().requires_grad_(True)
+    loss = ce(lg, lab)
+    timed(lambda: torch.autograd.grad(loss, lg, retain_graph=True), 2 * nl * vl * 2,
+          "ce_logits_backward f16 8192x50257")
+    del logits, lg, loss
+    vv = 16384 if args.rows_small else 128256
+    ids = torch.randint(0, vv, (n,), generator=g, device=dev)
+    touched = int(torch.unique(ids).numel())
+    gw = torch.zeros((vv, d), device=dev)
+    timed(lambda: embedding_scatter_add(gw, ids, x), n * d * 2 + touched * d * 8 + n * 24,
+          f"embedding_scatter_add f16 rows 32768x4096 -> fp32 {vv}x4096")
+    del gw
+    from nimbleml_b200.gpt_head import TiedEmbedding
+
+    te = TiedEmbedding(torch.randn((vv, d), generator=g, device=dev) * 0.02, vv, compute_dtype=torch.float16)
+    te.grad.normal_(generator=g)
+    timed(te.step, vv * d * 30, f"adamw_step fp32 master + fp16 copy {vv}x4096", reps=5)
+    del te
+    src = torch.randn((vv, d), generator=g, device=dev)
+    timed(lambda: k.round_tf32(src), vv * d * 8, f"round_tf32 {vv}x4096")
+    line = {"metric": "HBM-bound row kernels: achieved GB/s", "unit": "GB/s", "n_gpus": 1,
+            "peak": hbm, "peak_kind": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+            "timing": "CUDA events, mean of repeated launches after 3 warm-ups; inputs larger than L2",
+            "kernels": out}
     print(json.dumps(line), flush=True)
 
 
@@ -475,17 +569,27 @@ def main():
     ap.add_argument("--warmup-seconds", type=float, default=4.0,
                     help="keep warming up until this much time has passed, so every N is measured at "
                          "steady-state power and clocks")
-    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS) + ["c5"])
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS) + ["c5", "rows"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--rows-reps", type=int, default=20, help="--config rows: timed launches per kernel")
+    ap.add_argument("--rows-small", action="store_true",
+                    help="--config rows: a 16384-row vocabulary for the scatter / AdamW / rounding kernels "
+                         "(device footprint of a few GB, for profiler captures)")
     ap.add_argument("--shard-of", type=int, default=1,
                     help="profiling aid: one process computes rank 0's vocab shard of this many ranks through "
                          "the sharded backward entry point, with no collectives (not a bench line)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.config == "rows":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the row-kernel report has no reference arm"}))
+            return
+        run_rows(args)
+        return
     if args.config == "c5":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "config 5 is a GPU training harness; the "
