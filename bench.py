@@ -256,18 +256,55 @@ def run_reference_arm(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def full_loss64(h, e_local, labels, v_off, world, group, chunk=512):
+    """The mean loss over all N rows in float64, recomputed on the device a row
+    chunk at a time (never more than chunk x V_local logits); at P > 1 each
+    rank reduces its vocab shard and the per-row (max, sum-exp, target)
+    triples are merged over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    n = h.shape[0]
+    e64 = e_local.double()
+    v_local = e_local.shape[0]
+    st = torch.zeros((3, n), dtype=torch.float64, device=h.device)
+    for i in range(0, n, chunk):
+        s = h[i:i + chunk].double() @ e64.T
+        mx = s.max(1).values
+        st[0, i:i + chunk] = mx
+        st[1, i:i + chunk] = torch.exp(s - mx[:, None]).sum(1)
+        y = labels[i:i + chunk] - v_off
+        own = (y >= 0) & (y < v_local)
+        idx = own.nonzero()[:, 0]
+        st[2, i + idx] = s[idx, y[own]]
+        del s
+    if world > 1:
+        allst = torch.empty((world, 3, n), dtype=torch.float64, device=h.device)
+        dist.all_gather_into_tensor(allst, st, group=group)
+    else:
+        allst = st[None]
+    m = allst[:, 0].max(0).values
+    lse = m + torch.log((allst[:, 1] * torch.exp(allst[:, 0] - m)).sum(0))
+    return float((lse - allst[:, 2].sum(0)).mean())
+
+
 def sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss, dh, de, scale,
                    n_rows=32, n_cls=8):
     """Checks the last timed step's results on every rank against float64
-    recomputed on the device from the same inputs: sampled rows' lse and loss
-    terms (lse - target) at 2e-3, the loss as the mean of the per-row terms,
-    sampled rows of grad_hidden and sampled rows of this rank's grad_weights
-    shard at 1e-2 (relative 2-norm). Rank-local errors are maxed over ranks."""
+    recomputed on the device from the same inputs: the loss over all N rows,
+    sampled rows' lse and loss terms (lse - target), the loss as the mean of
+    the device's per-row terms, and sampled rows of grad_hidden and of this
+    rank's grad_weights shard (relative 2-norms). Tolerances follow the
+    compute dtype (fp16 / bf16: loss 2e-3, grads 1e-2; fp32 on TF32: loss
+    1e-5, grads 1e-3; per-row terms at ten times the loss tolerance, as the
+    loss averages their rounding). Rank-local errors are maxed over ranks."""
     import torch
     import torch.distributed as dist
 
     dev = h.device
     n = h.shape[0]
+    fp32 = h.dtype == torch.float32
+    loss64 = full_loss64(h, e_local, labels, v_off, world, group)
     g = torch.Generator(device="cpu").manual_seed(5)
     rows = torch.randperm(n, generator=g)[:n_rows].to(dev)
     e64 = e_local.double()
@@ -287,7 +324,8 @@ def sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss
     tgt = stats3[2].double().sum(0)                                      # (N,) target logit
     terms = lse.double() - tgt
     rel = lambda a, b: float((a - b).norm() / b.norm())
-    out = {"lse_rel": rel(lse.double()[rows], lse64), "loss_terms_rel": rel(terms[rows], terms64),
+    out = {"loss_rel": abs(float(loss) - loss64) / abs(loss64),
+           "lse_rel": rel(lse.double()[rows], lse64), "loss_terms_rel": rel(terms[rows], terms64),
            "loss_vs_mean_terms_rel": abs(float(loss) - float(terms.mean())) / float(terms.mean())}
     # grad_hidden rows: sum over shards of G_rows . E_shard (float64).
     gl = torch.exp(s_loc - lse64[:, None])
@@ -306,17 +344,18 @@ def sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss
     de_ref = (pc * (scale / n)).T @ h64
     out["de_rel"] = rel(de.double()[cls], de_ref)
     del h64, pc
-    errs = torch.tensor([out[k] for k in ("lse_rel", "loss_terms_rel", "loss_vs_mean_terms_rel", "dh_rel",
-                                          "de_rel")], dtype=torch.float64, device=dev)
+    keys = ("loss_rel", "lse_rel", "loss_terms_rel", "loss_vs_mean_terms_rel", "dh_rel", "de_rel")
+    errs = torch.tensor([out[k] for k in keys], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(errs, op=dist.ReduceOp.MAX, group=group)
-    keys = ("lse_rel", "loss_terms_rel", "loss_vs_mean_terms_rel", "dh_rel", "de_rel")
     out = {k: float(x) for k, x in zip(keys, errs.tolist())}
-    tol = {"lse_rel": 2e-3, "loss_terms_rel": 2e-3, "loss_vs_mean_terms_rel": 1e-5, "dh_rel": 1e-2,
-           "de_rel": 1e-2}
+    lt, gt = (1e-5, 1e-3) if fp32 else (2e-3, 1e-2)
+    tol = {"loss_rel": lt, "lse_rel": lt, "loss_terms_rel": 10 * lt, "loss_vs_mean_terms_rel": 1e-6,
+           "dh_rel": gt, "de_rel": gt}
     out["ok"] = all(out[k] <= tol[k] and math.isfinite(out[k]) for k in keys)
     out["tolerances"] = tol
-    out["sample"] = f"{n_rows} token rows, {n_cls} vocab rows per rank, float64 on the device, max over ranks"
+    out["sample"] = (f"loss over all {n} rows; {n_rows} token rows and {n_cls} vocab rows per rank sampled; float64 on "
+                     f"the device; max over ranks")
     return out
 
 
@@ -574,6 +613,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--also", default="c3,c2",
+                    help="with the default config 4: also device-time these configurations (comma list, '' for none)")
     ap.add_argument("--rows-reps", type=int, default=20, help="--config rows: timed launches per kernel")
     ap.add_argument("--rows-small", action="store_true",
                     help="--config rows: a 16384-row vocabulary for the scatter / AdamW / rounding kernels "
@@ -612,136 +653,151 @@ def main():
     rank, local, world = _dist_setup(args.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    dtype = getattr(torch, cfg["dtype"])
-    n, d, v = cfg["n"], cfg["d"], cfg["v"]
     group = dist.group.WORLD if world > 1 else None
-    emulate = args.shard_of if world == 1 and args.shard_of > 1 else 1
-    v_off, v_local = vp.shard_range(v, rank, world * emulate)
-    scale = GRAD_SCALE[cfg["dtype"]]
-
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1234)  # identical h / labels on every rank
-    h = torch.randn((n, d), generator=gen, device=dev, dtype=torch.float32)
-    if cfg["unit_rms"]:
-        h = h * torch.rsqrt(h.pow(2).mean(dim=1, keepdim=True))
-    h = h.to(dtype).contiguous()
-    labels = torch.randint(0, v, (n,), generator=gen, device=dev, dtype=torch.int64)
-    gen_e = torch.Generator(device=dev)
-    gen_e.manual_seed(99 + rank)
-    e_local = (torch.randn((v_local, d), generator=gen_e, device=dev) * 0.02).to(dtype).contiguous()
-    ign = k._NO_IGNORE
-    gscale = torch.full((1,), scale, device=dev)
-
-    # Per-phase CUDA events of the timed steps (current stream unless noted).
-    phases = []
-
-    def step(record=False):
-        ev = None
-        if record:
-            names = ["start", "fwd_end", "combine_end", "compute_end", "comm_start", "comm_end", "end"]
-            ev = {nm: torch.cuda.Event(enable_timing=True) for nm in names}
-            ev["start"].record()
-        rounded = (k.round_tf32(h), k.round_tf32(e_local)) if dtype == torch.float32 else None
-        part = k.shard_forward(*(rounded or (h, e_local)), labels, v_off, rounded=rounded is not None)
-        if record:
-            ev["fwd_end"].record()
-        stats3 = vp.gather_shard_stats(part, group)
-        _, _, lse, loss, valid = k.combine(stats3, labels, v, ign)
-        if record:
-            ev["combine_end"].record()
-        st = k.TiedCEStats(lse=lse, valid_count=valid, ignore_index=ign, vocab_size=v, vocab_offset=v_off,
-                           rounded=rounded)
-        if world > 1:
-            dh, de = vp.sharded_backward(gscale, h, e_local, labels, st, group, phase_events=ev)
-        elif emulate > 1:
-            ready = torch.cuda.Event()
-            sms = torch.cuda.get_device_properties(dev).multi_processor_count
-            dh, de = k.shard_backward(gscale, h, e_local, labels, st, grad_hidden_dtype=vp.dh_reduce_dtype(dtype),
-                                      ready_event=ready, last_de_max_ctas=max(1, sms - vp.COMM_SMS),
-                                      capped_fraction=vp.CAPPED_FRACTION)
-            if record:
-                ev["compute_end"].record()
-                ev["end"].record()
-        else:
-            dh, de = k.shard_backward(gscale, h, e_local, labels, st)
-            if record:
-                ev["compute_end"].record()
-                ev["end"].record()
-        if record:
-            phases.append(ev)
-        return stats3, lse, loss, dh, de
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # Warm-up: W steps, then more until --warmup-seconds have passed (the same
-    # count on every rank), so short multi-GPU runs are not timed before the
-    # GPUs reach their power-capped steady state.
-    t_w = time.perf_counter()
-    for _ in range(args.warmup):
-        step()
-    barrier()
-    per_step = (time.perf_counter() - t_w) / args.warmup
-    extra = max(0, math.ceil((args.warmup_seconds - (time.perf_counter() - t_w)) / max(per_step, 1e-4)))
-    if world > 1:
-        t = torch.tensor([extra], device=dev, dtype=torch.int64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        extra = int(t[0])
-    for _ in range(extra):
-        step()
-    barrier()
-    warmup_steps = args.warmup + extra
-    assert k.check_status(dev) == 0
-    bus = None
-    try:
-        pr = torch.cuda.get_device_properties(dev)
-        bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
-    except Exception:
-        pass
-    sampler = ClockSampler(bus) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
-    torch.cuda.reset_peak_memory_stats(dev)
-    mem0 = torch.cuda.memory_allocated(dev)
-    barrier()
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t_start.record()
-    for _ in range(args.steps):
-        last = step(record=True)
-    t_end.record()
-    barrier()
-    clocks = sampler.stop() if sampler else None
-    elapsed = t_start.elapsed_time(t_end) / 1e3
-    peak_extra = torch.cuda.max_memory_allocated(dev) - mem0
-    assert k.check_status(dev) == 0
+    def device_bench(cfg, steps, warmup, warmup_seconds, sample_clocks, do_parity):
+        """Device-timed steps of one configuration with inputs resident (the
+        `value` measurement); returns its inputs, timings and parity."""
+        dtype = getattr(torch, cfg["dtype"])
+        n, d, v = cfg["n"], cfg["d"], cfg["v"]
+        emulate = args.shard_of if world == 1 and args.shard_of > 1 else 1
+        v_off, v_local = vp.shard_range(v, rank, world * emulate)
+        scale = GRAD_SCALE[cfg["dtype"]]
 
-    def mean_ms(a, b):
-        return statistics.mean(ev[a].elapsed_time(ev[b]) for ev in phases)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1234)  # identical h / labels on every rank
+        h = torch.randn((n, d), generator=gen, device=dev, dtype=torch.float32)
+        if cfg["unit_rms"]:
+            h = h * torch.rsqrt(h.pow(2).mean(dim=1, keepdim=True))
+        h = h.to(dtype).contiguous()
+        labels = torch.randint(0, v, (n,), generator=gen, device=dev, dtype=torch.int64)
+        gen_e = torch.Generator(device=dev)
+        gen_e.manual_seed(99 + rank)
+        e_local = (torch.randn((v_local, d), generator=gen_e, device=dev) * 0.02).to(dtype).contiguous()
+        ign = k._NO_IGNORE
+        gscale = torch.full((1,), scale, device=dev)
 
-    phase_ms = {"forward_gemm_and_row_reduce": mean_ms("start", "fwd_end"),
-                "stats_exchange_and_combine": mean_ms("fwd_end", "combine_end"),
-                "backward_gemms": mean_ms("combine_end", "compute_end"),
-                "exposed_grad_hidden_reduction": mean_ms("compute_end", "end")}
-    if world > 1:
-        phase_ms["grad_hidden_all_reduce"] = mean_ms("comm_start", "comm_end")
-        phase_ms["all_reduce_start_after_backward_start"] = mean_ms("combine_end", "comm_start")
-    fwd_ms = phase_ms["forward_gemm_and_row_reduce"]
-    if world > 1:
-        keys = sorted(phase_ms)
-        t = torch.tensor([elapsed] + [phase_ms[x] for x in keys], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed = float(t[0])
-        phase_ms = {x: float(val) for x, val in zip(keys, t[1:].tolist())}
+        # Per-phase CUDA events of the timed steps (current stream unless noted).
+        phases = []
+
+        def step(record=False):
+            ev = None
+            if record:
+                names = ["start", "fwd_end", "combine_end", "compute_end", "comm_start", "comm_end", "end"]
+                ev = {nm: torch.cuda.Event(enable_timing=True) for nm in names}
+                ev["start"].record()
+            rounded = (k.round_tf32(h), k.round_tf32(e_local)) if dtype == torch.float32 else None
+            part = k.shard_forward(*(rounded or (h, e_local)), labels, v_off, rounded=rounded is not None)
+            if record:
+                ev["fwd_end"].record()
+            stats3 = vp.gather_shard_stats(part, group)
+            _, _, lse, loss, valid = k.combine(stats3, labels, v, ign)
+            if record:
+                ev["combine_end"].record()
+            st = k.TiedCEStats(lse=lse, valid_count=valid, ignore_index=ign, vocab_size=v, vocab_offset=v_off,
+                               rounded=rounded)
+            if world > 1:
+                dh, de = vp.sharded_backward(gscale, h, e_local, labels, st, group, phase_events=ev)
+            elif emulate > 1:
+                ready = torch.cuda.Event()
+                sms = torch.cuda.get_device_properties(dev).multi_processor_count
+                dh, de = k.shard_backward(gscale, h, e_local, labels, st, grad_hidden_dtype=vp.dh_reduce_dtype(dtype),
+                                          ready_event=ready, last_de_max_ctas=max(1, sms - vp.COMM_SMS),
+                                          capped_fraction=vp.CAPPED_FRACTION)
+                if record:
+                    ev["compute_end"].record()
+                    ev["end"].record()
+            else:
+                dh, de = k.shard_backward(gscale, h, e_local, labels, st)
+                if record:
+                    ev["compute_end"].record()
+                    ev["end"].record()
+            if record:
+                phases.append(ev)
+            return stats3, lse, loss, dh, de
+
+        # Warm-up: W steps, then more until --warmup-seconds have passed (the same
+        # count on every rank), so short multi-GPU runs are not timed before the
+        # GPUs reach their power-capped steady state.
+        t_w = time.perf_counter()
+        for _ in range(warmup):
+            step()
+        barrier()
+        per_step = (time.perf_counter() - t_w) / warmup
+        extra = max(0, math.ceil((warmup_seconds - (time.perf_counter() - t_w)) / max(per_step, 1e-4)))
+        if world > 1:
+            t = torch.tensor([extra], device=dev, dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            extra = int(t[0])
+        for _ in range(extra):
+            step()
+        barrier()
+        warmup_steps = warmup + extra
+        assert k.check_status(dev) == 0
+        bus = None
+        try:
+            pr = torch.cuda.get_device_properties(dev)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+        except Exception:
+            pass
+        sampler = ClockSampler(bus) if rank == 0 and sample_clocks else None
+        if sampler:
+            sampler.start()
+            time.sleep(0.3)
+        torch.cuda.reset_peak_memory_stats(dev)
+        mem0 = torch.cuda.memory_allocated(dev)
+        barrier()
+        t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_start.record()
+        for _ in range(steps):
+            last = step(record=True)
+        t_end.record()
+        barrier()
+        clocks = sampler.stop() if sampler else None
+        elapsed = t_start.elapsed_time(t_end) / 1e3
+        peak_extra = torch.cuda.max_memory_allocated(dev) - mem0
+        assert k.check_status(dev) == 0
+
+        def mean_ms(a, b):
+            return statistics.mean(ev[a].elapsed_time(ev[b]) for ev in phases)
+
+        phase_ms = {"forward_gemm_and_row_reduce": mean_ms("start", "fwd_end"),
+                    "stats_exchange_and_combine": mean_ms("fwd_end", "combine_end"),
+                    "backward_gemms": mean_ms("combine_end", "compute_end"),
+                    "exposed_grad_hidden_reduction": mean_ms("compute_end", "end")}
+        if world > 1:
+            phase_ms["grad_hidden_all_reduce"] = mean_ms("comm_start", "comm_end")
+            phase_ms["all_reduce_start_after_backward_start"] = mean_ms("combine_end", "comm_start")
         fwd_ms = phase_ms["forward_gemm_and_row_reduce"]
+        if world > 1:
+            keys = sorted(phase_ms)
+            t = torch.tensor([elapsed] + [phase_ms[x] for x in keys], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            elapsed = float(t[0])
+            phase_ms = {x: float(val) for x, val in zip(keys, t[1:].tolist())}
+            fwd_ms = phase_ms["forward_gemm_and_row_reduce"]
 
-    parity = None
-    if not args.no_parity and emulate == 1:
-        stats3, lse, loss, dh, de = last
-        parity = sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss, dh, de, scale)
-    del last
+        parity = None
+        if do_parity and emulate == 1:
+            stats3, lse, loss, dh, de = last
+            parity = sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss, dh, de, scale)
+        del last
+        return dict(h=h, labels=labels, e_local=e_local, v_off=v_off, v_local=v_local, scale=scale, dtype=dtype,
+                    elapsed=elapsed, phase_ms=phase_ms, fwd_ms=fwd_ms, parity=parity, peak_extra=peak_extra,
+                    clocks=clocks, warmup_steps=warmup_steps, emulate=emulate)
+
+    R = device_bench(cfg, args.steps, args.warmup, args.warmup_seconds, True, not args.no_parity)
+    h, labels, e_local, v_off, v_local = R["h"], R["labels"], R["e_local"], R["v_off"], R["v_local"]
+    scale, dtype, elapsed, phase_ms, fwd_ms = R["scale"], R["dtype"], R["elapsed"], R["phase_ms"], R["fwd_ms"]
+    parity, peak_extra, clocks, warmup_steps = R["parity"], R["peak_extra"], R["clocks"], R["warmup_steps"]
+    emulate = R["emulate"]
+    n, d, v = cfg["n"], cfg["d"], cfg["v"]
+    del R
 
     # ---- end to end through the public API: host inputs, H2D copy, loss D2H.
     e2e = None
@@ -802,10 +858,29 @@ def main():
                "h2d_bytes_per_step": h_host.numel() * h_host.element_size() // world + y_host.numel() * 8,
                "d2h_bytes_per_step": 4, "bytes_are": "per rank"}
 
+    # ---- the other configurations of the path, device-timed at the same N
+    # (config 3 fp16, config 2 fp32 on TF32), each with its own parity check.
+    also = {}
+    also_ok = True
+    if args.also and args.config == "c4" and emulate == 1:
+        for name in [x for x in args.also.split(",") if x]:
+            c = CONFIGS[name]
+            torch.cuda.empty_cache()
+            r = device_bench(c, 20, 3, 2.0, False, not args.no_parity)
+            st = r["elapsed"] / 20
+            also[name] = {"workload": c["workload"], "value": c["n"] / st, "unit": "tokens/s", "ms_per_step": st * 1e3,
+                          "steps": 20, "warmup": r["warmup_steps"], "dtype": DTYPE_TAG[c["dtype"]],
+                          "n_tokens": c["n"], "d_model": c["d"], "vocab": c["v"],
+                          "step_tflops_per_gpu": 8.0 * c["n"] * c["d"] * r["v_local"] / st / 1e12,
+                          "phases_ms": r["phase_ms"], "parity": r["parity"]}
+            if r["parity"] is not None and not r["parity"]["ok"]:
+                also_ok = False
+            del r
+
     if rank != 0:
         dist.barrier() if world > 1 else None
         dist.destroy_process_group() if world > 1 else None
-        if parity is not None and not parity["ok"]:
+        if (parity is not None and not parity["ok"]) or not also_ok:
             sys.exit(3)
         return
 
@@ -846,6 +921,7 @@ def main():
         "memory": {"peak_extra_bytes": int(peak_extra), "materialised_logits_bytes": n * v * h.element_size(),
                    "reference_style_peak_bytes": 3 * n * v * h.element_size()},
         "e2e": e2e,
+        "also": also or None,
     }
     if world == 1 and not args.no_cpu_baseline:
         step_fn, rows, sample, kind, threads = cpu_reference_sample(cfg)
@@ -859,8 +935,8 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    if parity is not None and not parity["ok"]:
-        print("parity check FAILED: " + json.dumps(parity), file=sys.stderr, flush=True)
+    if (parity is not None and not parity["ok"]) or not also_ok:
+        print("parity check FAILED: " + json.dumps({"headline": parity, "also": also}), file=sys.stderr, flush=True)
         sys.exit(3)
 
 
