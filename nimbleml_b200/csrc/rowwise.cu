@@ -17,6 +17,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <initializer_list>
 #include <string>
 #include <type_traits>
 
@@ -44,6 +45,45 @@ template <> __device__ __forceinline__ float from_f<float>(float v) { return v; 
 template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
+// Eight consecutive elements as fp32 (16-byte vector loads / stores; the
+// pointer must be 16-byte aligned for 16-bit types, 32-byte for fp32).
+template <typename T> __device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <> __device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <> __device__ __forceinline__ void load8<__half>(const __half* p, float (&v)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) { const float2 f = __half22float2(h[k]); v[2 * k] = f.x; v[2 * k + 1] = f.y; }
+}
+template <> __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) { const float2 f = __bfloat1622float2(h[k]); v[2 * k] = f.x; v[2 * k + 1] = f.y; }
+}
+template <typename T> __device__ __forceinline__ void store8(T* p, const float (&v)[8]);
+template <> __device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+template <> __device__ __forceinline__ void store8<__half>(__half* p, const float (&v)[8]) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <> __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
 // Running (max, sum of exp(x - max)) with one exp per element: the sum is
 // rescaled only when the maximum grows.
 struct OnlineLse {
@@ -56,6 +96,21 @@ struct OnlineLse {
     } else {
       s += ex2(d * kLog2e);
     }
+  }
+  // Adds n values with one rescale test for all of them.
+  template <int n>
+  __device__ __forceinline__ void add_n(const float* v) {
+    float vm = v[0];
+#pragma unroll
+    for (int k = 1; k < n; ++k) vm = fmaxf(vm, v[k]);
+    if (vm == -INFINITY) return;  // every value is -inf: nothing to add
+    if (vm > m) {
+      s = (m == -INFINITY) ? 0.0f : s * ex2((m - vm) * kLog2e);
+      m = vm;
+    }
+    const float ml2 = m * kLog2e;
+#pragma unroll
+    for (int k = 0; k < n; ++k) s += ex2(fmaf(v[k], kLog2e, -ml2));
   }
   __device__ __forceinline__ void merge(float m2, float s2) {
     if (m2 == -INFINITY) return;
@@ -82,12 +137,24 @@ __global__ void ce_rows_kernel(const T* __restrict__ x, int64_t ld, const int64_
   if ((reinterpret_cast<uintptr_t>(r) & 15) == 0) {
     const int64_t nvec = V / kVec;
     const uint4* r4 = reinterpret_cast<const uint4*>(r);
-    for (int64_t q = lane; q < nvec; q += 32) {
-      const uint4 u = __ldg(r4 + q);
+    auto add_vec = [&](const uint4& u) {
       const T* e = reinterpret_cast<const T*>(&u);
+      float v[kVec];
 #pragma unroll
-      for (int k = 0; k < kVec; ++k) acc.add(to_f<T>(e[k]));
+      for (int k = 0; k < kVec; ++k) v[k] = to_f<T>(e[k]);
+      acc.add_n<kVec>(v);
+    };
+    // Four 16-byte loads in flight per lane before any is used.
+    constexpr int kU = 4;
+    int64_t q = lane;
+    for (; q + 32 * (kU - 1) < nvec; q += 32 * kU) {
+      uint4 u[kU];
+#pragma unroll
+      for (int i = 0; i < kU; ++i) u[i] = __ldg(r4 + q + 32 * i);
+#pragma unroll
+      for (int i = 0; i < kU; ++i) add_vec(u[i]);
     }
+    for (; q < nvec; q += 32) add_vec(__ldg(r4 + q));
     j0 = nvec * kVec;
   }
   for (int64_t j = j0 + lane; j < V; j += 32) acc.add(to_f<T>(r[j]));
@@ -126,8 +193,7 @@ __global__ void ce_rows_grad_kernel(const T* __restrict__ x, int64_t ld, const i
   int64_t j0 = 0;
   if ((reinterpret_cast<uintptr_t>(r) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
     const int64_t nvec = V / kVec;
-    for (int64_t q = lane; q < nvec; q += 32) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(r) + q);
+    auto grad_vec = [&](const uint4& u, int64_t q) {
       const T* e = reinterpret_cast<const T*>(&u);
       uint4 w;
       T* f = reinterpret_cast<T*>(&w);
@@ -139,7 +205,17 @@ __global__ void ce_rows_grad_kernel(const T* __restrict__ x, int64_t ld, const i
         f[k] = from_f<T>(p * scale);
       }
       reinterpret_cast<uint4*>(o)[q] = w;
+    };
+    constexpr int kU = 4;
+    int64_t q = lane;
+    for (; q + 32 * (kU - 1) < nvec; q += 32 * kU) {
+      uint4 u[kU];
+#pragma unroll
+      for (int i = 0; i < kU; ++i) u[i] = __ldg(reinterpret_cast<const uint4*>(r) + q + 32 * i);
+#pragma unroll
+      for (int i = 0; i < kU; ++i) grad_vec(u[i], q + 32 * i);
     }
+    for (; q < nvec; q += 32) grad_vec(__ldg(reinterpret_cast<const uint4*>(r) + q), q);
     j0 = nvec * kVec;
   }
   for (int64_t j = j0 + lane; j < V; j += 32) {
@@ -287,6 +363,105 @@ rmsnorm_bwd_kernel(const GT* __restrict__ grad, const T* __restrict__ x, const T
   }
 }
 
+// Vector forms of the two RMSNorm kernels for d % 8 == 0 and 16-byte aligned
+// rows: thread t of the block owns the 8-element vectors t, t + 256, ...
+// (KV of them), so every load and store is 16 bytes wide.
+template <typename T, int KV>
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_fwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ gamma, int64_t N, int d, float eps,
+                       T* __restrict__ y, float* __restrict__ out_ms, float* __restrict__ out_rms) {
+  __shared__ float red[kNormThreads / 32];
+  const int nv = d / 8;
+  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+    const T* xr = x + row * d;
+    float xv[KV][8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < KV; ++k) {
+      const int q = threadIdx.x + k * kNormThreads;
+      if (q < nv) {
+        load8<T>(xr + 8 * q, xv[k]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(xv[k][e], xv[k][e], ss);
+      }
+    }
+    const float ms = block_sum(ss, red) / static_cast<float>(d);
+    const float rms = sqrtf(ms + eps);
+    const float inv = 1.0f / rms;
+#pragma unroll
+    for (int k = 0; k < KV; ++k) {
+      const int q = threadIdx.x + k * kNormThreads;
+      if (q < nv) {
+        float gv[8], yv[8];
+        load8<T>(gamma + 8 * q, gv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) yv[e] = xv[k][e] * inv * gv[e];
+        store8<T>(y + row * d + 8 * q, yv);
+      }
+    }
+    if (threadIdx.x == 0) {
+      out_ms[row] = ms;
+      out_rms[row] = rms;
+    }
+  }
+}
+
+template <typename T, typename GT, int KV>
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_bwd_vec_kernel(const GT* __restrict__ grad, const T* __restrict__ x, const T* __restrict__ gamma,
+                       const float* __restrict__ ms, const float* __restrict__ rms, int64_t N, int d, float eps,
+                       T* __restrict__ gx, float* __restrict__ partial) {
+  __shared__ float red[kNormThreads / 32];
+  const int nv = d / 8;
+  float gm[KV][8], gg[KV][8];
+#pragma unroll
+  for (int k = 0; k < KV; ++k) {
+    const int q = threadIdx.x + k * kNormThreads;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) gm[k][e] = gg[k][e] = 0.0f;
+    if (q < nv) load8<T>(gamma + 8 * q, gm[k]);
+  }
+  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+    float gv[KV][8], xv[KV][8];
+    float dot = 0.0f;
+#pragma unroll
+    for (int k = 0; k < KV; ++k) {
+      const int q = threadIdx.x + k * kNormThreads;
+      if (q < nv) {
+        load8<GT>(grad + row * d + 8 * q, gv[k]);
+        load8<T>(x + row * d + 8 * q, xv[k]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dot = fmaf(gv[k][e] * gm[k][e], xv[k][e], dot);
+      }
+    }
+    dot = block_sum(dot, red);
+    const float inv = 1.0f / rms[row];
+    const float msv = ms[row] + eps;
+    const float coef = (2.0f / static_cast<float>(d)) * (-0.5f) * dot / (msv * sqrtf(msv));
+#pragma unroll
+    for (int k = 0; k < KV; ++k) {
+      const int q = threadIdx.x + k * kNormThreads;
+      if (q < nv) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          o[e] = gv[k][e] * gm[k][e] * inv + xv[k][e] * coef;
+          gg[k][e] = fmaf(gv[k][e], xv[k][e] * inv, gg[k][e]);
+        }
+        store8<T>(gx + row * d + 8 * q, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < KV; ++k) {
+    const int q = threadIdx.x + k * kNormThreads;
+    if (q < nv) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) partial[static_cast<int64_t>(blockIdx.x) * d + 8 * q + e] = gg[k][e];
+    }
+  }
+}
+
 // grad_gamma[j] (+)= sum over blocks b = 0..G-1 of partial[b, j], in order.
 __global__ void sum_partials_kernel(const float* __restrict__ partial, int G, int d, float* __restrict__ out,
                                     int accumulate) {
@@ -320,13 +495,26 @@ __global__ void scatter_keys_kernel(const int64_t* __restrict__ ids, int64_t n, 
 template <typename T>
 __global__ void scatter_segments_kernel(float* __restrict__ gw, const uint32_t* __restrict__ keys,
                                         const int32_t* __restrict__ rows, const T* __restrict__ go, int64_t n,
-                                        uint32_t sentinel, int d) {
+                                        uint32_t sentinel, int d, bool vec) {
   for (int64_t b = blockIdx.x; b < n; b += gridDim.x) {
     const uint32_t key = keys[b];
     if (key == sentinel || (b > 0 && keys[b - 1] == key)) continue;  // not the first row of a group
     int64_t e = b + 1;
     while (e < n && keys[e] == key) ++e;
     float* dst = gw + static_cast<int64_t>(key) * d;
+    if (vec) {  // 8 columns per thread and step, 16-byte loads and stores
+      for (int j = 8 * threadIdx.x; j < d; j += 8 * blockDim.x) {
+        float acc[8], g[8];
+        load8<float>(dst + j, acc);
+        for (int64_t p = b; p < e; ++p) {
+          load8<T>(go + static_cast<int64_t>(rows[p]) * d + j, g);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[k] += g[k];
+        }
+        store8<float>(dst + j, acc);
+      }
+      continue;
+    }
     for (int j = threadIdx.x; j < d; j += blockDim.x) {
       float acc = dst[j];
       for (int64_t p = b; p < e; ++p) acc += to_f<T>(go[static_cast<int64_t>(rows[p]) * d + j]);
@@ -350,6 +538,35 @@ __global__ void adamw_kernel(float* __restrict__ w, const G* __restrict__ g, flo
     v[i] = vn;
     w[i] = wn;
     if (copy) copy[i] = from_f<P>(wn);
+  }
+}
+
+// The same update, 8 elements per thread and step with 16-byte accesses (n a
+// multiple of 8, every pointer 16-byte aligned).
+template <typename G, typename P>
+__global__ void adamw_vec_kernel(float* __restrict__ w, const G* __restrict__ g, float* __restrict__ m,
+                                 float* __restrict__ v, int64_t n8, float lr, float b1, float b2, float bc1,
+                                 float bc2, float eps, float wd, P* __restrict__ copy) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float wv[8], gv[8], mv[8], vv[8];
+    load8<float>(w + 8 * i, wv);
+    load8<G>(g + 8 * i, gv);
+    load8<float>(m + 8 * i, mv);
+    load8<float>(v + 8 * i, vv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float mn = b1 * mv[k] + (1.0f - b1) * gv[k];
+      const float vn = b2 * vv[k] + (1.0f - b2) * gv[k] * gv[k];
+      const float upd = (mn / bc1) / (sqrtf(vn / bc2) + eps);
+      mv[k] = mn;
+      vv[k] = vn;
+      wv[k] = wv[k] * (1.0f - lr * wd) - lr * upd;
+    }
+    store8<float>(w + 8 * i, wv);
+    store8<float>(m + 8 * i, mv);
+    store8<float>(v + 8 * i, vv);
+    if (copy) store8<P>(copy + 8 * i, wv);
   }
 }
 
@@ -469,6 +686,15 @@ extern "C" int nimble_sampled_ce_backward(const float* grad_scale, const float* 
 namespace {
 constexpr int kNormMaxD = 32 * kNormThreads;  // 8192
 int norm_grid(int64_t N) { return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(N, 2 * 148))); }
+// The vector kernels keep more rows in flight: several blocks per SM.
+int norm_vec_grid(int64_t N) { return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(N, 6 * 148))); }
+// 8-element vectors: d a multiple of 8 and every base pointer 16-byte aligned.
+bool vec_rows_ok(int d, std::initializer_list<const void*> ptrs) {
+  if (d % 8 != 0) return false;
+  for (const void* p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) & 15) return false;
+  return true;
+}
 }  // namespace
 
 extern "C" int nimble_rmsnorm_forward(const void* x, const void* gamma, int64_t n_rows, int64_t d_model, float eps,
@@ -485,7 +711,15 @@ extern "C" int nimble_rmsnorm_forward(const void* x, const void* gamma, int64_t 
     const T* xt = static_cast<const T*>(x);
     const T* gt = static_cast<const T*>(gamma);
     T* yt = static_cast<T*>(y);
-    if (d <= 4 * kNormThreads)
+    if (vec_rows_ok(d, {x, gamma, y})) {
+      const int vgrid = norm_vec_grid(n_rows);
+      if (d <= 8 * kNormThreads)
+        rmsnorm_fwd_vec_kernel<T, 1><<<vgrid, kNormThreads, 0, s>>>(xt, gt, n_rows, d, eps, yt, out_ms, out_rms);
+      else if (d <= 16 * kNormThreads)
+        rmsnorm_fwd_vec_kernel<T, 2><<<vgrid, kNormThreads, 0, s>>>(xt, gt, n_rows, d, eps, yt, out_ms, out_rms);
+      else
+        rmsnorm_fwd_vec_kernel<T, 4><<<vgrid, kNormThreads, 0, s>>>(xt, gt, n_rows, d, eps, yt, out_ms, out_rms);
+    } else if (d <= 4 * kNormThreads)
       rmsnorm_fwd_kernel<T, 4><<<grid, kNormThreads, 0, s>>>(xt, gt, n_rows, d, eps, yt, out_ms, out_rms);
     else if (d <= 16 * kNormThreads)
       rmsnorm_fwd_kernel<T, 16><<<grid, kNormThreads, 0, s>>>(xt, gt, n_rows, d, eps, yt, out_ms, out_rms);
@@ -498,7 +732,8 @@ extern "C" int nimble_rmsnorm_forward(const void* x, const void* gamma, int64_t 
 
 extern "C" int nimble_rmsnorm_backward_workspace_size(int64_t n_rows, int64_t d_model, size_t* bytes) {
   if (!bytes || n_rows < 0 || d_model <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "bad arguments");
-  *bytes = sizeof(float) * static_cast<size_t>(norm_grid(n_rows)) * static_cast<size_t>(d_model);
+  *bytes = sizeof(float) * static_cast<size_t>(std::max(norm_grid(n_rows), norm_vec_grid(n_rows))) *
+           static_cast<size_t>(d_model);
   return NIMBLE_OK;
 }
 
@@ -517,7 +752,8 @@ extern "C" int nimble_rmsnorm_backward(const void* grad, const void* x, const vo
   }
   if (!grad || !x || !gamma || !ms || !rms || !grad_x || !grad_gamma)
     return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
-  const int grid = norm_grid(n_rows);
+  const bool vec = vec_rows_ok(d, {grad, x, gamma, grad_x});
+  const int grid = vec ? norm_vec_grid(n_rows) : norm_grid(n_rows);
   if (!workspace || workspace_bytes < sizeof(float) * static_cast<size_t>(grid) * d)
     return fail(NIMBLE_ERR_WORKSPACE, "rmsnorm backward workspace too small");
   float* partial = static_cast<float*>(workspace);
@@ -530,6 +766,18 @@ extern "C" int nimble_rmsnorm_backward(const void* grad, const void* x, const vo
     T* gxt = static_cast<T*>(grad_x);
     auto launch = [&](auto gt) {
       using GT = std::remove_cv_t<std::remove_pointer_t<decltype(gt)>>;
+      if (vec) {
+        if (d <= 8 * kNormThreads)
+          rmsnorm_bwd_vec_kernel<T, GT, 1><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt,
+                                                                        partial);
+        else if (d <= 16 * kNormThreads)
+          rmsnorm_bwd_vec_kernel<T, GT, 2><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt,
+                                                                        partial);
+        else
+          rmsnorm_bwd_vec_kernel<T, GT, 4><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt,
+                                                                        partial);
+        return;
+      }
       if (d <= 4 * kNormThreads)
         rmsnorm_bwd_kernel<T, GT, 4><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
       else if (d <= 16 * kNormThreads)
@@ -623,7 +871,8 @@ extern "C" int nimble_embedding_scatter_add(float* grad_weights, const int64_t* 
   NIMBLE_DISPATCH(grad_out_dtype, T,
                   scatter_segments_kernel<T><<<grid, threads, 0, s>>>(
                       grad_weights, keys_out, rows_out, static_cast<const T*>(grad_out), n_rows,
-                      static_cast<uint32_t>(vocab_rows), static_cast<int>(d_model)));
+                      static_cast<uint32_t>(vocab_rows), static_cast<int>(d_model),
+                      vec_rows_ok(static_cast<int>(d_model), {grad_weights, grad_out})));
   NIMBLE_CUDA_TRY(cudaGetLastError());
   return NIMBLE_OK;
 }
@@ -640,12 +889,18 @@ extern "C" int nimble_adamw_step(float* weights, const void* grad, int grad_dtyp
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = grid_for(n, 256);
   const int cdt = weights_copy ? weights_copy_dtype : NIMBLE_DTYPE_F32;
+  const bool vec = n % 8 == 0 && vec_rows_ok(8, {weights, grad, exp_avg, exp_avg_sq, weights_copy});
   NIMBLE_DISPATCH(grad_dtype, G, {
-    NIMBLE_DISPATCH(cdt, P,
-                    adamw_kernel<G, P><<<grid, 256, 0, s>>>(weights, static_cast<const G*>(grad), exp_avg,
-                                                            exp_avg_sq, n, lr, beta1, beta2, bias_correction1,
-                                                            bias_correction2, eps, weight_decay,
-                                                            static_cast<P*>(weights_copy)));
+    NIMBLE_DISPATCH(cdt, P, {
+      if (vec)
+        adamw_vec_kernel<G, P><<<grid_for(n / 8, 256), 256, 0, s>>>(
+            weights, static_cast<const G*>(grad), exp_avg, exp_avg_sq, n / 8, lr, beta1, beta2, bias_correction1,
+            bias_correction2, eps, weight_decay, static_cast<P*>(weights_copy));
+      else
+        adamw_kernel<G, P><<<grid, 256, 0, s>>>(weights, static_cast<const G*>(grad), exp_avg, exp_avg_sq, n, lr,
+                                                beta1, beta2, bias_correction1, bias_correction2, eps, weight_decay,
+                                                static_cast<P*>(weights_copy));
+    });
   });
   NIMBLE_CUDA_TRY(cudaGetLastError());
   return NIMBLE_OK;
