@@ -121,107 +121,99 @@ struct OnlineLse {
   }
 };
 
-// One warp per row of a [N x V] logits matrix (row pitch ld): the row's
-// max, sum-exp and the label's logit (0 when the label is outside [0, V)).
+// One block of kRowThreads per row of a [N x V] logits matrix (row pitch ld):
+// the row's max, sum-exp and the label's logit (0 when the label is outside
+// [0, V)). Each thread folds 16-byte vectors into a running (max, sum-exp);
+// warps merge by shuffles, the block through shared memory.
+constexpr int kRowThreads = 256;
 template <typename T>
-__global__ void ce_rows_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restrict__ labels, int64_t N,
-                               int64_t V, float* __restrict__ out_max, float* __restrict__ out_sum,
-                               float* __restrict__ out_tgt) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
-  if (row >= N) return;
-  const T* r = x + row * ld;
-  OnlineLse acc;
-  constexpr int kVec = 16 / sizeof(T);
-  int64_t j0 = 0;
-  if ((reinterpret_cast<uintptr_t>(r) & 15) == 0) {
-    const int64_t nvec = V / kVec;
-    const uint4* r4 = reinterpret_cast<const uint4*>(r);
-    auto add_vec = [&](const uint4& u) {
-      const T* e = reinterpret_cast<const T*>(&u);
-      float v[kVec];
+__global__ void __launch_bounds__(kRowThreads)
+ce_rows_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restrict__ labels, int64_t N, int64_t V,
+               float* __restrict__ out_max, float* __restrict__ out_sum, float* __restrict__ out_tgt) {
+  __shared__ float sm_m[kRowThreads / 32], sm_s[kRowThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+    const T* r = x + row * ld;
+    OnlineLse acc;
+    constexpr int kVec = 16 / sizeof(T);
+    int64_t j0 = 0;
+    if ((reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+      const int64_t nvec = V / kVec;
+      const uint4* r4 = reinterpret_cast<const uint4*>(r);
+      for (int64_t q = threadIdx.x; q < nvec; q += kRowThreads) {
+        const uint4 u = __ldg(r4 + q);
+        const T* e = reinterpret_cast<const T*>(&u);
+        float v[kVec];
 #pragma unroll
-      for (int k = 0; k < kVec; ++k) v[k] = to_f<T>(e[k]);
-      acc.add_n<kVec>(v);
-    };
-    // Four 16-byte loads in flight per lane before any is used.
-    constexpr int kU = 4;
-    int64_t q = lane;
-    for (; q + 32 * (kU - 1) < nvec; q += 32 * kU) {
-      uint4 u[kU];
-#pragma unroll
-      for (int i = 0; i < kU; ++i) u[i] = __ldg(r4 + q + 32 * i);
-#pragma unroll
-      for (int i = 0; i < kU; ++i) add_vec(u[i]);
+        for (int k = 0; k < kVec; ++k) v[k] = to_f<T>(e[k]);
+        acc.add_n<kVec>(v);
+      }
+      j0 = nvec * kVec;
     }
-    for (; q < nvec; q += 32) add_vec(__ldg(r4 + q));
-    j0 = nvec * kVec;
-  }
-  for (int64_t j = j0 + lane; j < V; j += 32) acc.add(to_f<T>(r[j]));
+    for (int64_t j = j0 + threadIdx.x; j < V; j += kRowThreads) acc.add(to_f<T>(r[j]));
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, acc.m, off);
-    const float s2 = __shfl_xor_sync(0xffffffffu, acc.s, off);
-    acc.merge(m2, s2);
-  }
-  if (lane == 0) {
-    out_max[row] = acc.m;
-    out_sum[row] = acc.s;
-    const int64_t lab = labels[row];
-    out_tgt[row] = (lab >= 0 && lab < V) ? to_f<T>(r[lab]) : 0.0f;
+    for (int off = 16; off > 0; off >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, acc.m, off);
+      const float s2 = __shfl_xor_sync(0xffffffffu, acc.s, off);
+      acc.merge(m2, s2);
+    }
+    if (lane == 0) {
+      sm_m[warp] = acc.m;
+      sm_s[warp] = acc.s;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      OnlineLse t;
+      for (int w = 0; w < kRowThreads / 32; ++w) t.merge(sm_m[w], sm_s[w]);
+      out_max[row] = t.m;
+      out_sum[row] = t.s;
+      const int64_t lab = labels[row];
+      out_tgt[row] = (lab >= 0 && lab < V) ? to_f<T>(r[lab]) : 0.0f;
+    }
+    __syncthreads();
   }
 }
 
 // grad[i, j] = (exp(x_ij - lse_i) - [j == y_i]) * grad_scale / n_valid, rows
 // with y_i == ignore_index all zero. One warp per row.
 template <typename T>
-__global__ void ce_rows_grad_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restrict__ labels,
-                                    const float* __restrict__ lse, int64_t N, int64_t V, int64_t ignore_index,
-                                    const float* __restrict__ grad_scale, const float* __restrict__ valid_count,
-                                    T* __restrict__ g, int64_t ldg) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
-  if (row >= N) return;
+__global__ void __launch_bounds__(kRowThreads)
+ce_rows_grad_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restrict__ labels,
+                    const float* __restrict__ lse, int64_t N, int64_t V, int64_t ignore_index,
+                    const float* __restrict__ grad_scale, const float* __restrict__ valid_count,
+                    T* __restrict__ g, int64_t ldg) {
   const float nv = *valid_count;
-  const int64_t lab = labels[row];
-  const bool live = lab != ignore_index && lab >= 0 && lab < V && nv > 0.0f;
-  const float scale = live ? *grad_scale / nv : 0.0f;
-  const float l2 = live ? lse[row] * kLog2e : 0.0f;
-  const T* r = x + row * ld;
-  T* o = g + row * ldg;
-  constexpr int kVec = 16 / sizeof(T);
-  int64_t j0 = 0;
-  if ((reinterpret_cast<uintptr_t>(r) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-    const int64_t nvec = V / kVec;
-    auto grad_vec = [&](const uint4& u, int64_t q) {
-      const T* e = reinterpret_cast<const T*>(&u);
-      uint4 w;
-      T* f = reinterpret_cast<T*>(&w);
+  for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+    const int64_t lab = labels[row];
+    const bool live = lab != ignore_index && lab >= 0 && lab < V && nv > 0.0f;
+    const float scale = live ? *grad_scale / nv : 0.0f;
+    const float l2 = live ? lse[row] * kLog2e : 0.0f;
+    const T* r = x + row * ld;
+    T* o = g + row * ldg;
+    constexpr int kVec = 16 / sizeof(T);
+    int64_t j0 = 0;
+    if ((reinterpret_cast<uintptr_t>(r) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+      const int64_t nvec = V / kVec;
+      for (int64_t q = threadIdx.x; q < nvec; q += kRowThreads) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(r) + q);
+        const T* e = reinterpret_cast<const T*>(&u);
+        uint4 w;
+        T* f = reinterpret_cast<T*>(&w);
 #pragma unroll
-      for (int k = 0; k < kVec; ++k) {
-        const int64_t j = q * kVec + k;
-        float p = live ? ex2(fmaf(to_f<T>(e[k]), kLog2e, -l2)) : 0.0f;
-        if (j == lab) p -= 1.0f;
-        f[k] = from_f<T>(p * scale);
+        for (int k = 0; k < kVec; ++k) {
+          float p = live ? ex2(fmaf(to_f<T>(e[k]), kLog2e, -l2)) : 0.0f;
+          if (q * kVec + k == lab) p -= 1.0f;
+          f[k] = from_f<T>(p * scale);
+        }
+        reinterpret_cast<uint4*>(o)[q] = w;
       }
-      reinterpret_cast<uint4*>(o)[q] = w;
-    };
-    constexpr int kU = 4;
-    int64_t q = lane;
-    for (; q + 32 * (kU - 1) < nvec; q += 32 * kU) {
-      uint4 u[kU];
-#pragma unroll
-      for (int i = 0; i < kU; ++i) u[i] = __ldg(reinterpret_cast<const uint4*>(r) + q + 32 * i);
-#pragma unroll
-      for (int i = 0; i < kU; ++i) grad_vec(u[i], q + 32 * i);
+      j0 = nvec * kVec;
     }
-    for (; q < nvec; q += 32) grad_vec(__ldg(reinterpret_cast<const uint4*>(r) + q), q);
-    j0 = nvec * kVec;
-  }
-  for (int64_t j = j0 + lane; j < V; j += 32) {
-    float p = live ? ex2(fmaf(to_f<T>(r[j]), kLog2e, -l2)) : 0.0f;
-    if (j == lab) p -= 1.0f;
-    o[j] = from_f<T>(p * scale);
+    for (int64_t j = j0 + threadIdx.x; j < V; j += kRowThreads) {
+      float p = live ? ex2(fmaf(to_f<T>(r[j]), kLog2e, -l2)) : 0.0f;
+      if (j == lab) p -= 1.0f;
+      o[j] = from_f<T>(p * scale);
+    }
   }
 }
 
@@ -284,6 +276,20 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   float t = 0.0f;
 #pragma unroll
   for (int i = 0; i < kNormThreads / 32; ++i) t += red[i];
+  return t;
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_sum_n(float v, float* red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < THREADS / 32; ++i) t += red[i];
   return t;
 }
 
@@ -406,17 +412,17 @@ rmsnorm_fwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ gamma, int
   }
 }
 
-template <typename T, typename GT, int KV>
-__global__ void __launch_bounds__(kNormThreads)
+template <typename T, typename GT, int KV, int THREADS>
+__global__ void __launch_bounds__(THREADS)
 rmsnorm_bwd_vec_kernel(const GT* __restrict__ grad, const T* __restrict__ x, const T* __restrict__ gamma,
                        const float* __restrict__ ms, const float* __restrict__ rms, int64_t N, int d, float eps,
                        T* __restrict__ gx, float* __restrict__ partial) {
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[THREADS / 32];
   const int nv = d / 8;
   float gm[KV][8], gg[KV][8];
 #pragma unroll
   for (int k = 0; k < KV; ++k) {
-    const int q = threadIdx.x + k * kNormThreads;
+    const int q = threadIdx.x + k * THREADS;
 #pragma unroll
     for (int e = 0; e < 8; ++e) gm[k][e] = gg[k][e] = 0.0f;
     if (q < nv) load8<T>(gamma + 8 * q, gm[k]);
@@ -426,7 +432,7 @@ rmsnorm_bwd_vec_kernel(const GT* __restrict__ grad, const T* __restrict__ x, con
     float dot = 0.0f;
 #pragma unroll
     for (int k = 0; k < KV; ++k) {
-      const int q = threadIdx.x + k * kNormThreads;
+      const int q = threadIdx.x + k * THREADS;
       if (q < nv) {
         load8<GT>(grad + row * d + 8 * q, gv[k]);
         load8<T>(x + row * d + 8 * q, xv[k]);
@@ -434,13 +440,13 @@ rmsnorm_bwd_vec_kernel(const GT* __restrict__ grad, const T* __restrict__ x, con
         for (int e = 0; e < 8; ++e) dot = fmaf(gv[k][e] * gm[k][e], xv[k][e], dot);
       }
     }
-    dot = block_sum(dot, red);
+    dot = block_sum_n<THREADS>(dot, red);
     const float inv = 1.0f / rms[row];
     const float msv = ms[row] + eps;
     const float coef = (2.0f / static_cast<float>(d)) * (-0.5f) * dot / (msv * sqrtf(msv));
 #pragma unroll
     for (int k = 0; k < KV; ++k) {
-      const int q = threadIdx.x + k * kNormThreads;
+      const int q = threadIdx.x + k * THREADS;
       if (q < nv) {
         float o[8];
 #pragma unroll
@@ -454,7 +460,7 @@ rmsnorm_bwd_vec_kernel(const GT* __restrict__ grad, const T* __restrict__ x, con
   }
 #pragma unroll
   for (int k = 0; k < KV; ++k) {
-    const int q = threadIdx.x + k * kNormThreads;
+    const int q = threadIdx.x + k * THREADS;
     if (q < nv) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) partial[static_cast<int64_t>(blockIdx.x) * d + 8 * q + e] = gg[k][e];
@@ -604,10 +610,9 @@ extern "C" int nimble_ce_logits_forward(const void* logits, int64_t row_pitch, c
     return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (n_rows > 0) {
-    const int rows_per_block = 8;
-    const unsigned grid = static_cast<unsigned>((n_rows + rows_per_block - 1) / rows_per_block);
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(n_rows, 148 * 64));
     NIMBLE_DISPATCH(dtype, T,
-                    ce_rows_kernel<T><<<grid, 32 * rows_per_block, 0, s>>>(
+                    ce_rows_kernel<T><<<grid, kRowThreads, 0, s>>>(
                         static_cast<const T*>(logits), row_pitch, labels, n_rows, n_classes, out_max, out_sumexp,
                         out_target));
     NIMBLE_CUDA_TRY(cudaGetLastError());
@@ -626,10 +631,9 @@ extern "C" int nimble_ce_logits_backward(const float* grad_scale, const float* v
   if (!grad_scale || !valid_count || !labels || !lse || !grad_logits)
     return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int rows_per_block = 8;
-  const unsigned grid = static_cast<unsigned>((n_rows + rows_per_block - 1) / rows_per_block);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(n_rows, 148 * 64));
   NIMBLE_DISPATCH(dtype, T,
-                  ce_rows_grad_kernel<T><<<grid, 32 * rows_per_block, 0, s>>>(
+                  ce_rows_grad_kernel<T><<<grid, kRowThreads, 0, s>>>(
                       static_cast<const T*>(logits), row_pitch, labels, lse, n_rows, n_classes, ignore_index,
                       grad_scale, valid_count, static_cast<T*>(grad_logits), grad_row_pitch));
   NIMBLE_CUDA_TRY(cudaGetLastError());
@@ -732,8 +736,7 @@ extern "C" int nimble_rmsnorm_forward(const void* x, const void* gamma, int64_t 
 
 extern "C" int nimble_rmsnorm_backward_workspace_size(int64_t n_rows, int64_t d_model, size_t* bytes) {
   if (!bytes || n_rows < 0 || d_model <= 0) return fail(NIMBLE_ERR_INVALID_ARG, "bad arguments");
-  *bytes = sizeof(float) * static_cast<size_t>(std::max(norm_grid(n_rows), norm_vec_grid(n_rows))) *
-           static_cast<size_t>(d_model);
+  *bytes = sizeof(float) * static_cast<size_t>(norm_grid(n_rows)) * static_cast<size_t>(d_model);
   return NIMBLE_OK;
 }
 
@@ -753,7 +756,7 @@ extern "C" int nimble_rmsnorm_backward(const void* grad, const void* x, const vo
   if (!grad || !x || !gamma || !ms || !rms || !grad_x || !grad_gamma)
     return fail(NIMBLE_ERR_INVALID_ARG, "null pointer argument");
   const bool vec = vec_rows_ok(d, {grad, x, gamma, grad_x});
-  const int grid = vec ? norm_vec_grid(n_rows) : norm_grid(n_rows);
+  const int grid = norm_grid(n_rows);
   if (!workspace || workspace_bytes < sizeof(float) * static_cast<size_t>(grid) * d)
     return fail(NIMBLE_ERR_WORKSPACE, "rmsnorm backward workspace too small");
   float* partial = static_cast<float*>(workspace);
@@ -766,16 +769,12 @@ extern "C" int nimble_rmsnorm_backward(const void* grad, const void* x, const vo
     T* gxt = static_cast<T*>(grad_x);
     auto launch = [&](auto gt) {
       using GT = std::remove_cv_t<std::remove_pointer_t<decltype(gt)>>;
-      if (vec) {
-        if (d <= 8 * kNormThreads)
-          rmsnorm_bwd_vec_kernel<T, GT, 1><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt,
-                                                                        partial);
-        else if (d <= 16 * kNormThreads)
-          rmsnorm_bwd_vec_kernel<T, GT, 2><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt,
-                                                                        partial);
+      if (vec) {  // 512 threads, one or two 8-element vectors each
+        constexpr int kT = 2 * kNormThreads;
+        if (d <= 8 * kT)
+          rmsnorm_bwd_vec_kernel<T, GT, 1, kT><<<grid, kT, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
         else
-          rmsnorm_bwd_vec_kernel<T, GT, 4><<<grid, kNormThreads, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt,
-                                                                        partial);
+          rmsnorm_bwd_vec_kernel<T, GT, 2, kT><<<grid, kT, 0, s>>>(gt, xt, gm, ms, rms, n_rows, d, eps, gxt, partial);
         return;
       }
       if (d <= 4 * kNormThreads)
