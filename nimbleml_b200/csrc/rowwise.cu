@@ -136,19 +136,33 @@ ce_rows_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restrict__ 
     const T* r = x + row * ld;
     OnlineLse acc;
     constexpr int kVec = 16 / sizeof(T);
-    int64_t j0 = 0;
-    if ((reinterpret_cast<uintptr_t>(r) & 15) == 0) {
-      const int64_t nvec = V / kVec;
-      const uint4* r4 = reinterpret_cast<const uint4*>(r);
-      for (int64_t q = threadIdx.x; q < nvec; q += kRowThreads) {
-        const uint4 u = __ldg(r4 + q);
+    // Rows of an odd-width matrix start off the 16-byte grid: the first
+    // `head` elements go one by one, the rest in 16-byte vectors.
+    const int64_t head = min(V, static_cast<int64_t>(((16 - (reinterpret_cast<uintptr_t>(r) & 15)) & 15) / sizeof(T)));
+    for (int64_t j = threadIdx.x; j < head; j += kRowThreads) acc.add(to_f<T>(r[j]));
+    int64_t j0 = head;
+    if (((reinterpret_cast<uintptr_t>(r + head)) & 15) == 0) {
+      const int64_t nvec = (V - head) / kVec;
+      const uint4* r4 = reinterpret_cast<const uint4*>(r + head);
+      auto add_vec = [&](const uint4& u) {
         const T* e = reinterpret_cast<const T*>(&u);
         float v[kVec];
 #pragma unroll
         for (int k = 0; k < kVec; ++k) v[k] = to_f<T>(e[k]);
         acc.add_n<kVec>(v);
+      };
+      // kU 16-byte loads in flight per thread before the first is used.
+      constexpr int kU = 4;
+      int64_t q = threadIdx.x;
+      for (; q + (kU - 1) * kRowThreads < nvec; q += kU * kRowThreads) {
+        uint4 u[kU];
+#pragma unroll
+        for (int i = 0; i < kU; ++i) u[i] = __ldg(r4 + q + i * kRowThreads);
+#pragma unroll
+        for (int i = 0; i < kU; ++i) add_vec(u[i]);
       }
-      j0 = nvec * kVec;
+      for (; q < nvec; q += kRowThreads) add_vec(__ldg(r4 + q));
+      j0 = head + nvec * kVec;
     }
     for (int64_t j = j0 + threadIdx.x; j < V; j += kRowThreads) acc.add(to_f<T>(r[j]));
 #pragma unroll
@@ -191,29 +205,45 @@ ce_rows_grad_kernel(const T* __restrict__ x, int64_t ld, const int64_t* __restri
     const T* r = x + row * ld;
     T* o = g + row * ldg;
     constexpr int kVec = 16 / sizeof(T);
+    auto grad_one = [&](int64_t j) {
+      float p = live ? ex2(fmaf(to_f<T>(r[j]), kLog2e, -l2)) : 0.0f;
+      if (j == lab) p -= 1.0f;
+      o[j] = from_f<T>(p * scale);
+    };
+    // Odd-width rows: scalar head up to the 16-byte grid, then vectors, when
+    // input and output rows sit at the same offset from it.
+    const uintptr_t mis = reinterpret_cast<uintptr_t>(r) & 15;
+    const int64_t head = min(V, static_cast<int64_t>(((16 - mis) & 15) / sizeof(T)));
     int64_t j0 = 0;
-    if ((reinterpret_cast<uintptr_t>(r) & 15) == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-      const int64_t nvec = V / kVec;
-      for (int64_t q = threadIdx.x; q < nvec; q += kRowThreads) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(r) + q);
+    if (mis == (reinterpret_cast<uintptr_t>(o) & 15) && (mis % sizeof(T)) == 0) {
+      for (int64_t j = threadIdx.x; j < head; j += kRowThreads) grad_one(j);
+      const int64_t nvec = (V - head) / kVec;
+      const uint4* r4 = reinterpret_cast<const uint4*>(r + head);
+      auto grad_vec = [&](const uint4& u, int64_t q) {
         const T* e = reinterpret_cast<const T*>(&u);
         uint4 w;
         T* f = reinterpret_cast<T*>(&w);
 #pragma unroll
         for (int k = 0; k < kVec; ++k) {
           float p = live ? ex2(fmaf(to_f<T>(e[k]), kLog2e, -l2)) : 0.0f;
-          if (q * kVec + k == lab) p -= 1.0f;
+          if (head + q * kVec + k == lab) p -= 1.0f;
           f[k] = from_f<T>(p * scale);
         }
-        reinterpret_cast<uint4*>(o)[q] = w;
+        reinterpret_cast<uint4*>(o + head)[q] = w;
+      };
+      constexpr int kU = 2;
+      int64_t q = threadIdx.x;
+      for (; q + (kU - 1) * kRowThreads < nvec; q += kU * kRowThreads) {
+        uint4 u[kU];
+#pragma unroll
+        for (int i = 0; i < kU; ++i) u[i] = __ldg(r4 + q + i * kRowThreads);
+#pragma unroll
+        for (int i = 0; i < kU; ++i) grad_vec(u[i], q + i * kRowThreads);
       }
-      j0 = nvec * kVec;
+      for (; q < nvec; q += kRowThreads) grad_vec(__ldg(r4 + q), q);
+      j0 = head + nvec * kVec;
     }
-    for (int64_t j = j0 + threadIdx.x; j < V; j += kRowThreads) {
-      float p = live ? ex2(fmaf(to_f<T>(r[j]), kLog2e, -l2)) : 0.0f;
-      if (j == lab) p -= 1.0f;
-      o[j] = from_f<T>(p * scale);
-    }
+    for (int64_t j = j0 + threadIdx.x; j < V; j += kRowThreads) grad_one(j);
   }
 }
 
