@@ -360,6 +360,11 @@ def sampled_parity(h, e_local, labels, v, v_off, world, group, stats3, lse, loss
 
 
 def run_c5(args):
+    """`--config c5`: prints config 5's own JSON line (see c5_measure)."""
+    print(json.dumps(c5_measure(args.steps, args.warmup)), flush=True)
+
+
+def c5_measure(steps, warmup):
     """Config 5: one GPT training step (24 layers, d=1024, 16 heads, seq 1024,
     batch 8, V=50257, fp16 autocast) with clip_grad_norm(1.0) and AdamW;
     reports the head's share of step time and memory.
@@ -440,7 +445,7 @@ def run_c5(args):
         return loss
 
     def timed(fn, k):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -451,7 +456,7 @@ def run_c5(args):
         torch.cuda.synchronize()
         return a.elapsed_time(b) / k
 
-    step_ms = timed(step, args.steps)
+    step_ms = timed(step, steps)
     torch.cuda.reset_peak_memory_stats(dev)
     step()
     torch.cuda.synchronize()
@@ -488,12 +493,12 @@ def run_c5(args):
         torch.cuda.synchronize()
         return torch.cuda.max_memory_allocated(dev) - base
 
-    head_ms = timed(head_ours, args.steps)
-    torch_ms = timed(head_torch, args.steps)
+    head_ms = timed(head_ours, steps)
+    torch_ms = timed(head_torch, steps)
     line = {
         "metric": "GPT training step tokens/s (config 5: 24L, d=1024, V=50257, batch 8 x 1024, fp16)",
-        "value": B * S / (step_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "dtype": "f16",
+        "value": B * S / (step_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+        "warmup": warmup, "ms_per_step": step_ms, "higher_is_better": True, "dtype": "f16",
         "data": "synthetic, random init",
         "config": {"workload": "config 5 harness: torch trunk; this library's tied embedding (lookup, shared fp32 "
                                "grad, deterministic scatter), final RMSNorm fused with the tied head, AdamW",
@@ -507,7 +512,9 @@ def run_c5(args):
                  "head_tflops": 8.0 * B * S * D * V / (head_ms / 1e3) / 1e12},
         "step_peak_bytes": int(step_peak),
     }
-    print(json.dumps(line), flush=True)
+    del model, opt
+    torch.cuda.empty_cache()
+    return line
 
 
 def run_rows(args):
@@ -615,6 +622,8 @@ def main():
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--also", default="c3,c2",
                     help="with the default config 4: also device-time these configurations (comma list, '' for none)")
+    ap.add_argument("--no-c5", dest="also_c5", action="store_false",
+                    help="with the default config 4 on one GPU: skip the config-5 training-step measurement")
     ap.add_argument("--rows-reps", type=int, default=20, help="--config rows: timed launches per kernel")
     ap.add_argument("--rows-small", action="store_true",
                     help="--config rows: a 16384-row vocabulary for the scatter / AdamW / rounding kernels "
@@ -876,6 +885,10 @@ def main():
             if r["parity"] is not None and not r["parity"]["ok"]:
                 also_ok = False
             del r
+        if world == 1 and args.also_c5:
+            # Config 5: one GPT training step (one GPU) around this library's head.
+            torch.cuda.empty_cache()
+            also["c5"] = c5_measure(5, 3)
 
     if rank != 0:
         dist.barrier() if world > 1 else None
