@@ -106,3 +106,59 @@ def test_hidden_from_host_assembles_all_rows():
     want = torch.arange(13 * 4, dtype=torch.float32).view(13, 4)
     for _, got in res:
         assert torch.equal(got, want)
+
+
+def _lookup_worker(rank, world, port, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nimbleml_b200.gpt_head import TiedEmbedding
+        from nimbleml_b200.vocab_parallel import shard_range
+
+        v, d = 37, 8  # uneven shards
+        e = torch.arange(v * d, dtype=torch.float32).reshape(v, d) / 7.0
+        off, rows = shard_range(v, rank, world)
+        te = TiedEmbedding(e[off:off + rows].clone(), v, vocab_offset=off, compute_dtype=torch.float32,
+                           group=dist.group.WORLD)
+        ids = torch.tensor([[0, 36, 18, 19], [5, 5, 30, 17]])
+        out = te.lookup(ids).detach()
+        result_q.put((rank, out.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_vocab_parallel_lookup_assembles_every_row_exactly():
+    """The tied embedding's vocab-parallel lookup: each rank gathers its own
+    rows (zeros elsewhere) and one all_reduce assembles exact rows everywhere."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29300 + os.getpid() % 500
+    procs = [ctx.Process(target=_lookup_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=120) for _ in range(world)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    e = torch.arange(37 * 8, dtype=torch.float32).reshape(37, 8) / 7.0
+    ids = torch.tensor([[0, 36, 18, 19], [5, 5, 30, 17]])
+    for _, out in res:
+        assert np.array_equal(out, e[ids].numpy())
+
+
+def test_tied_embedding_argument_checks():
+    from nimbleml_b200.gpt_head import TiedEmbedding
+    from nimbleml_b200.vocab_parallel import dh_reduce_dtype
+
+    with pytest.raises(ValueError, match="float32"):
+        TiedEmbedding(torch.zeros((4, 8), dtype=torch.float16), 10)
+    with pytest.raises(ValueError, match="inside the vocabulary"):
+        TiedEmbedding(torch.zeros((4, 8)), 10, vocab_offset=8)
+    te = TiedEmbedding(torch.ones((4, 8)), 10, vocab_offset=6, compute_dtype=torch.float16)
+    assert te.weight.dtype == torch.float16 and te.grad.dtype == torch.float32 and te.rows == 4
+    # The grad_hidden reduction dtype: bf16 partials for 16-bit inputs, fp32 for fp32.
+    assert dh_reduce_dtype(torch.float16) == torch.bfloat16
+    assert dh_reduce_dtype(torch.bfloat16) == torch.bfloat16
+    assert dh_reduce_dtype(torch.float32) == torch.float32
