@@ -817,36 +817,43 @@ def main():
         head = vp.VocabParallelTiedHead(None, v, group=group, shard=w_param) if world > 1 else None
         lossfn = CrossEntropyLoss()
 
-        # Single GPU: inputs are double-buffered on the device and step i+1's
-        # host-to-device copies run on a side stream while step i computes (a
-        # prefetching input pipeline; every timed step still copies its own
-        # inputs). Several GPUs: each rank copies 1/P of h, NVLink all_gather
-        # assembles the rest.
+        # Inputs are double-buffered on the device and step i+1's copies run on
+        # a side stream while step i computes (a prefetching input pipeline;
+        # every timed step still copies its own inputs). Several GPUs: each
+        # rank copies 1/P of h from the host, an NVLink all_gather assembles
+        # the rest.
         copy_stream = torch.cuda.Stream(dev)
+        main_stream = torch.cuda.current_stream(dev)
         hbuf = [torch.empty_like(h) for _ in range(2)]
         ybuf = [torch.empty_like(labels) for _ in range(2)]
         ready = [torch.cuda.Event() for _ in range(2)]
 
         def prefetch(i):
             with torch.cuda.stream(copy_stream):
-                hbuf[i % 2].copy_(h_host, non_blocking=True)
+                if head is None:
+                    hbuf[i % 2].copy_(h_host, non_blocking=True)
+                else:
+                    # This rank's 1/P of the rows from pinned host memory, the
+                    # rest by one NVLink all_gather (NCCL keeps collectives in
+                    # issue order, so it cannot cross the backward's all_reduce).
+                    full = head.hidden_from_host(h_host)
+                    full.record_stream(main_stream)  # used there by step i
+                    hbuf[i % 2] = full
                 ybuf[i % 2].copy_(y_host, non_blocking=True)
                 ready[i % 2].record(copy_stream)
 
         def e2e_step(i, k):
             w_param.grad = None
+            if i == 0:
+                prefetch(0)
+            if i + 1 < k:
+                prefetch(i + 1)  # buffer (i+1)%2 is free: step i-1 ended with a host sync
+            torch.cuda.current_stream(dev).wait_event(ready[i % 2])
+            hd = hbuf[i % 2].detach().requires_grad_(True)
+            yd = ybuf[i % 2]
             if head is None:
-                if i == 0:
-                    prefetch(0)
-                if i + 1 < k:
-                    prefetch(i + 1)  # buffer (i+1)%2 is free: step i-1 ended with a host sync
-                torch.cuda.current_stream(dev).wait_event(ready[i % 2])
-                hd = hbuf[i % 2].detach().requires_grad_(True)
-                yd = ybuf[i % 2]
                 loss = lossfn.forward_tied(hd.view(cfg["batch"], cfg["seq"], d), w_param, yd)
             else:
-                hd = head.hidden_from_host(h_host).requires_grad_(True)
-                yd = y_host.to(dev, non_blocking=True)
                 loss = head.loss(hd, yd)
             (loss * scale).backward()  # the same loss scale as the device-timed step
             return float(loss)
