@@ -253,6 +253,16 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&r)[32]
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Ties the destination registers of an earlier tcgen05.ld to this point:
+// placed after tmem_wait_ld, it keeps the compiler from reading them before
+// the wait (to the compiler they are defined at the load instruction).
+__device__ __forceinline__ void tmem_fence_regs(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8)
+    asm volatile("" : "+r"(r[i]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), "+r"(r[i + 4]), "+r"(r[i + 5]),
+                 "+r"(r[i + 6]), "+r"(r[i + 7]));
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA
 // with 128-byte swizzle: rows of 128 B, 8-row swizzle atoms 1024 B apart.
 // Field layout (tcgen05 shared memory descriptor): start address >> 4 in

@@ -391,6 +391,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           __syncwarp();
           ptx::tmem_ld_32cols(tbase + c * 32, r);
           ptx::tmem_wait_ld();
+          ptx::tmem_fence_regs(r);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -451,6 +452,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           __syncwarp();
           ptx::tmem_ld_32cols(tbase + c * 32, r);
           ptx::tmem_wait_ld();
+          ptx::tmem_fence_regs(r);
           const int jt = tcol - c * 32;
           float v[32];
 #pragma unroll
@@ -485,6 +487,7 @@ tc_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           __syncwarp();
           ptx::tmem_ld_32cols(tbase + c * 32, r);
           ptx::tmem_wait_ld();
+          ptx::tmem_fence_regs(r);
           if (!row_ok) continue;
           const int64_t col = col0_tile + c * 32;
           const int nv = min(32, ncols - c * 32);
